@@ -1,0 +1,173 @@
+/*
+ * ncz_flash.h -- C ABI of the B200 (sm_100a) flash-attention forward library
+ * (libncz_flash.so).  It is a drop-in for the `flash` module of not-cute-zig.
+ *
+ * All pointers passed to the launch entry points are DEVICE pointers owned by
+ * the caller; the library never frees them.  Launches are asynchronous on the
+ * given stream (NULL = the legacy default stream).  Validation happens before
+ * any launch, and nothing is launched when it fails.  No function prints.
+ *
+ * Tensor layout (the reference's, src/flash.zig:5-15): Q/K/V are f16, O is f32
+ * (f16 optional through ncz_flash_fwd_ex).  batch_heads independent slices
+ * start at slice * *_stride elements; inside a slice, row r starts at
+ * r * row_stride elements, where row_stride is head_dim in the reference API.
+ */
+#ifndef NCZ_FLASH_H
+#define NCZ_FLASH_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Return codes.  0..15 mirror the reference's CudaError set one to one
+ * (src/cuda.zig:134-151, mapping at src/cuda.zig:160-177).  16..17 are new:
+ * a bounded in-kernel wait expired, and an alignment the chosen path needs is
+ * missing (only returned when a caller forces the TMA path). */
+typedef enum ncz_status {
+    NCZ_SUCCESS = 0,
+    NCZ_ERROR_OUT_OF_MEMORY = 1,
+    NCZ_ERROR_OVERFLOW = 2,
+    NCZ_ERROR_SHARED_OBJECT_INIT_FAILED = 3,
+    NCZ_ERROR_NOT_FOUND = 4,
+    NCZ_ERROR_INVALID_VALUE = 5,
+    NCZ_ERROR_INVALID_CONTEXT = 6,
+    NCZ_ERROR_INVALID_DEVICE = 7,
+    NCZ_ERROR_INVALID_IMAGE = 8,
+    NCZ_ERROR_CONTEXT_IS_DESTROYED = 9,
+    NCZ_ERROR_LAUNCH_FAILED = 10,
+    NCZ_ERROR_LAUNCH_OUT_OF_RESOURCES = 11,
+    NCZ_ERROR_LAUNCH_TIMEOUT = 12,
+    NCZ_ERROR_ILLEGAL_ADDRESS = 13,
+    NCZ_ERROR_NO_DEVICE = 14,
+    NCZ_ERROR_NOT_INITIALIZED = 15,
+    NCZ_ERROR_UNKNOWN = 16,
+    NCZ_ERROR_DEVICE_TIMEOUT = 17,
+    NCZ_ERROR_MISALIGNED = 18
+} ncz_status;
+
+/* Output element type. */
+typedef enum ncz_dtype { NCZ_DTYPE_F32 = 0, NCZ_DTYPE_F16 = 1 } ncz_dtype;
+
+/* Producer selection: AUTO picks the TMA path when every Q/K/V base pointer is
+ * 16-byte aligned and every Q/K/V stride is a multiple of 8 elements, and the
+ * load/store-unit (LSU) path otherwise.  Both are the same sm_100a kernel
+ * (tcgen05 MMAs, TMEM accumulators); they differ only in how K/V/Q tiles
+ * reach shared memory. */
+typedef enum ncz_producer {
+    NCZ_PRODUCER_AUTO = 0,
+    NCZ_PRODUCER_TMA = 1,
+    NCZ_PRODUCER_LSU = 2
+} ncz_producer;
+
+/* Extended descriptor (ncz_flash_fwd_ex).  Zero row strides mean head_dim
+ * (the reference layout).  Fields mirror flash.Options (src/flash.zig:5-15)
+ * plus: per-row strides, O element type, producer override, device ordinal
+ * (-1 = current device) and stream. */
+typedef struct ncz_flash_desc {
+    const void *q;
+    const void *k;
+    const void *v;
+    void *o;
+    size_t batch_heads;
+    size_t seq_len;
+    size_t head_dim;
+    size_t q_stride, k_stride, v_stride, o_stride;                 /* per slice, elements */
+    size_t q_row_stride, k_row_stride, v_row_stride, o_row_stride; /* per row, 0 = head_dim */
+    float scale;
+    uint32_t causal;
+    int32_t o_dtype;  /* ncz_dtype */
+    int32_t producer; /* ncz_producer */
+    int32_t device;   /* CUDA ordinal, -1 = current */
+    void *stream;     /* cudaStream_t / CUstream, NULL = default stream */
+} ncz_flash_desc;
+
+/* Loads nothing eagerly; resolves the driver entry points and records the
+ * device count.  Idempotent.  Called implicitly by every launch. */
+int ncz_init(void);
+/* Drops cached per-device state.  Kernels in flight are not waited for. */
+int ncz_shutdown(void);
+
+/* flash.Options.validate (src/flash.zig:16-28): batch_heads > 0, seq_len > 0,
+ * head_dim in {16,32,64}, every slice stride >= seq_len * head_dim. */
+int ncz_flash_validate(size_t batch_heads, size_t seq_len, size_t head_dim, size_t q_stride,
+                       size_t k_stride, size_t v_stride, size_t o_stride);
+
+/* Validation of the extended descriptor: the reference rules with row strides
+ * (each row stride >= head_dim, each slice stride >= (seq_len-1)*row_stride +
+ * head_dim), o_dtype and producer in range. */
+int ncz_flash_validate_ex(const ncz_flash_desc *desc);
+
+/* flash.selectKernel (src/flash.zig:72-96).  Writes the kernel label (e.g.
+ * "flash_fwd_sm100a_d64_tma") into `label` (NUL-terminated, truncated to
+ * `cap`) and the threads per CTA into *threads.  One sm_100a kernel family
+ * replaces flash_attention_fwd_{opt,v2,h64,h64_bn32,h64_causal}. */
+int ncz_flash_select(size_t batch_heads, size_t seq_len, size_t head_dim, uint32_t causal,
+                     char *label, size_t cap, uint32_t *threads);
+
+/* The reference kernel argument tuple (src/flash.zig:55-68, the 12 arguments
+ * of flash_attention_fwd_* plus batch_heads and a stream).  Replaces
+ * selectKernel + Function.launch (src/main.zig:820-852, :1022-1035) and the
+ * exported kernel symbols (src/main_device.zig:19-47).  Q/K/V f16, O f32. */
+int ncz_flash_fwd(const void *q, const void *k, const void *v, void *o, size_t batch_heads,
+                  size_t seq_len, size_t head_dim, size_t q_stride, size_t k_stride,
+                  size_t v_stride, size_t o_stride, float scale, uint32_t causal, void *stream);
+
+/* flash.launch (src/flash.zig:31-70): like ncz_flash_fwd, but takes the
+ * slice lengths (elements) so requireLen (src/flash.zig:98-100) is checked:
+ * each length must be >= batch_heads * stride. */
+int ncz_flash_launch(const void *q, size_t q_len, const void *k, size_t k_len, const void *v,
+                     size_t v_len, void *o, size_t o_len, size_t batch_heads, size_t seq_len,
+                     size_t head_dim, size_t q_stride, size_t k_stride, size_t v_stride,
+                     size_t o_stride, float scale, uint32_t causal, void *stream);
+
+/* Extended launch: row strides, f16 O, producer override, device ordinal.
+ * No reference counterpart beyond flash.launch (src/flash.zig:31-70). */
+int ncz_flash_fwd_ex(const ncz_flash_desc *desc);
+
+/* One call, several devices: descs[i] is launched on descs[i].device (each on
+ * its own stream); the caller's current device is restored.  Used to shard
+ * batch x head slices across GPUs.  The reference has one device only
+ * (src/cuda.zig:181-196); this replaces a per-device loop over flash.launch. */
+int ncz_flash_fwd_multi(const ncz_flash_desc *descs, int count);
+
+/* Synchronises `stream` (on `device`, -1 = current), then reads and clears the
+ * device's in-kernel status word.  Returns NCZ_ERROR_DEVICE_TIMEOUT when a
+ * bounded wait expired in a kernel since the last call, a CUDA error code
+ * when the stream faulted, NCZ_SUCCESS otherwise.  *detail (may be NULL)
+ * receives the raw status word (0 if clean). */
+int ncz_flash_sync_status(int device, void *stream, uint32_t *detail);
+
+/* Human-readable name of a status code (static storage). */
+const char *ncz_status_string(int status);
+
+/* Number of kernel launches this library has issued in this process
+ * (all devices).  Used by benchmarks to report their own launch count. */
+uint64_t ncz_launch_count(void);
+
+/* --- Host-side helpers used by unit tests (no device work). --- */
+
+/* tcgen05 shared-memory matrix descriptor (64-bit) for a tile at shared
+ * address `smem_addr`: layout_type is the UMMA swizzle code (0 none, 2 =
+ * 128B, 4 = 64B, 6 = 32B); lbo/sbo in bytes.  Extends the warp-MMA
+ * Descriptor of src/mma.zig:23-57 to the sm_100 shared-memory descriptor. */
+uint64_t ncz_umma_smem_desc(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                            uint32_t layout_type);
+
+/* tcgen05 kind::f16 instruction descriptor: f16 A/B, f32 accumulate, given
+ * M, N and operand majors (0 = K-major, 1 = MN-major). */
+uint32_t ncz_umma_instr_desc_f16(uint32_t m, uint32_t n, uint32_t a_major, uint32_t b_major);
+
+/* Byte-address swizzle of a TMA SWIZZLE_{32,64,128}B tile: the shared-memory
+ * byte offset at which logical byte offset `offset` of a tile with
+ * `span_bytes` (32, 64 or 128) wide rows is stored.  Generalises
+ * layout.XorSwizzle (src/layout.zig:327-358) from element to byte offsets. */
+uint32_t ncz_tma_swizzle_offset(uint32_t span_bytes, uint32_t offset);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NCZ_FLASH_H */

@@ -1,0 +1,15 @@
+"""not-cute-zig B200: an sm_100a flash-attention forward behind the reference's
+`flash` module API (src/flash.zig).  The package directory name is not a
+Python identifier, so import it with importlib.import_module("not-cute-zig_b200").
+"""
+from . import flash  # noqa: F401
+from .flash import (  # noqa: F401
+    FlashError,
+    KernelSelection,
+    Options,
+    launch,
+    launch_ex,
+    launch_multi,
+    select_kernel,
+    sync_status,
+)

@@ -1,0 +1,423 @@
+// flash_api.cu -- the C ABI of libncz_flash.so (declared in include/ncz_flash.h).
+//
+// Host side of the drop-in for not-cute-zig's `flash` module:
+//   Options.validate  src/flash.zig:16-28   -> ncz_flash_validate
+//   launch/requireLen src/flash.zig:31-70,98-100 -> ncz_flash_launch / ncz_flash_fwd
+//   selectKernel      src/flash.zig:72-96   -> ncz_flash_select
+//   CudaError/check   src/cuda.zig:134-178  -> ncz_status / map_cuda_error
+// The driver wrapper's single context (src/cuda.zig:181-196) becomes the
+// runtime's per-device primary contexts; cuTensorMapEncodeTiled is resolved
+// through cudaGetDriverEntryPointByVersion so the library has no link-time
+// dependency on libcuda (it loads on machines without a GPU driver).
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <atomic>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "flash_fwd_sm100.cuh"
+#include "ncz_flash.h"
+
+namespace {
+
+using ncz::FlashParams;
+using ncz::SmemLayout;
+
+constexpr int kMaxDevices = 64;
+constexpr int kVariants = 6;  // (D in 16/32/64) x (TMA, LSU)
+
+std::mutex g_mu;
+bool g_init_done = false;
+int g_init_status = NCZ_ERROR_NOT_INITIALIZED;
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::atomic<uint64_t> g_launches{0};
+bool g_attr_done[kMaxDevices][kVariants];
+
+int map_cuda_error(cudaError_t e) {
+    switch (e) {
+        case cudaSuccess: return NCZ_SUCCESS;
+        case cudaErrorMemoryAllocation: return NCZ_ERROR_OUT_OF_MEMORY;
+        case cudaErrorSharedObjectInitFailed: return NCZ_ERROR_SHARED_OBJECT_INIT_FAILED;
+        case cudaErrorSymbolNotFound: return NCZ_ERROR_NOT_FOUND;
+        case cudaErrorInvalidValue: return NCZ_ERROR_INVALID_VALUE;
+        case cudaErrorDeviceUninitialized: return NCZ_ERROR_INVALID_CONTEXT;
+        case cudaErrorInvalidDevice: return NCZ_ERROR_INVALID_DEVICE;
+        case cudaErrorInvalidKernelImage:
+        case cudaErrorNoKernelImageForDevice: return NCZ_ERROR_INVALID_IMAGE;
+        case cudaErrorContextIsDestroyed: return NCZ_ERROR_CONTEXT_IS_DESTROYED;
+        case cudaErrorLaunchFailure: return NCZ_ERROR_LAUNCH_FAILED;
+        case cudaErrorLaunchOutOfResources: return NCZ_ERROR_LAUNCH_OUT_OF_RESOURCES;
+        case cudaErrorLaunchTimeout: return NCZ_ERROR_LAUNCH_TIMEOUT;
+        case cudaErrorIllegalAddress: return NCZ_ERROR_ILLEGAL_ADDRESS;
+        case cudaErrorNoDevice: return NCZ_ERROR_NO_DEVICE;
+        case cudaErrorInitializationError:
+        case cudaErrorInsufficientDriver: return NCZ_ERROR_NOT_INITIALIZED;
+        default: return NCZ_ERROR_UNKNOWN;
+    }
+}
+
+// Fully resolved launch description: row strides defaulted, dtype checked.
+struct Resolved {
+    const void *q, *k, *v;
+    void *o;
+    size_t bh, seq, d;
+    size_t qs, ks, vs, os;      // slice strides
+    size_t qr, kr, vr, orow;    // row strides
+    float scale;
+    uint32_t causal;
+    int o_dtype;
+    int producer;
+    int device;
+    cudaStream_t stream;
+};
+
+bool mul_ok(size_t a, size_t b, size_t *out) { return !__builtin_mul_overflow(a, b, out); }
+
+// The reference rule (src/flash.zig:16-28), generalised to row strides:
+// the last element a slice touches is (seq-1)*row + d - 1 < stride.
+int validate_resolved(const Resolved &r) {
+    if (r.bh == 0 || r.seq == 0) return NCZ_ERROR_INVALID_VALUE;
+    if (r.d != 16 && r.d != 32 && r.d != 64) return NCZ_ERROR_INVALID_VALUE;
+    const size_t rows[4] = {r.qr, r.kr, r.vr, r.orow};
+    const size_t slices[4] = {r.qs, r.ks, r.vs, r.os};
+    for (int i = 0; i < 4; ++i) {
+        if (rows[i] < r.d) return NCZ_ERROR_INVALID_VALUE;
+        size_t span;
+        if (!mul_ok(r.seq - 1, rows[i], &span) || span + r.d < span) return NCZ_ERROR_OVERFLOW;
+        if (slices[i] < span + r.d) return NCZ_ERROR_INVALID_VALUE;
+        size_t total;
+        if (!mul_ok(slices[i], r.bh, &total)) return NCZ_ERROR_OVERFLOW;
+    }
+    if (r.o_dtype != NCZ_DTYPE_F32 && r.o_dtype != NCZ_DTYPE_F16) return NCZ_ERROR_INVALID_VALUE;
+    if (r.producer < NCZ_PRODUCER_AUTO || r.producer > NCZ_PRODUCER_LSU) return NCZ_ERROR_INVALID_VALUE;
+    // Implementation limits of the 32-bit tile / grid indices.
+    if (r.seq > (size_t(1) << 30)) return NCZ_ERROR_INVALID_VALUE;
+    const size_t pairs = (r.seq + 255) / 256;
+    size_t grid;
+    if (!mul_ok(pairs, r.bh, &grid) || grid > size_t(0x7FFFFFFF)) return NCZ_ERROR_INVALID_VALUE;
+    if (r.bh > size_t(0x7FFFFFFF)) return NCZ_ERROR_INVALID_VALUE;
+    return NCZ_SUCCESS;
+}
+
+Resolved from_desc(const ncz_flash_desc &d) {
+    Resolved r;
+    r.q = d.q; r.k = d.k; r.v = d.v; r.o = d.o;
+    r.bh = d.batch_heads; r.seq = d.seq_len; r.d = d.head_dim;
+    r.qs = d.q_stride; r.ks = d.k_stride; r.vs = d.v_stride; r.os = d.o_stride;
+    r.qr = d.q_row_stride ? d.q_row_stride : d.head_dim;
+    r.kr = d.k_row_stride ? d.k_row_stride : d.head_dim;
+    r.vr = d.v_row_stride ? d.v_row_stride : d.head_dim;
+    r.orow = d.o_row_stride ? d.o_row_stride : d.head_dim;
+    r.scale = d.scale; r.causal = d.causal;
+    r.o_dtype = d.o_dtype; r.producer = d.producer; r.device = d.device;
+    r.stream = static_cast<cudaStream_t>(d.stream);
+    return r;
+}
+
+bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// 3-D map over one operand: dims (d, seq, bh), box (d, 128, 1), swizzle = row width.
+bool encode_map(CUtensorMap *map, const void *ptr, size_t d, size_t seq, size_t bh, size_t row, size_t slice) {
+    cuuint64_t dims[3] = {d, seq, bh};
+    cuuint64_t strides[2] = {row * 2, slice * 2};
+    cuuint32_t box[3] = {static_cast<cuuint32_t>(d), 128u, 1u};
+    cuuint32_t estr[3] = {1u, 1u, 1u};
+    const CUtensorMapSwizzle swz = d == 64 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                           : (d == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+    const CUresult res = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(ptr), dims, strides,
+                                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return res == CUDA_SUCCESS;
+}
+
+template <int D, bool kTma>
+int launch_variant(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv, const FlashParams &p,
+                   unsigned grid, int dev, cudaStream_t stream) {
+    using L = SmemLayout<D>;
+    auto kernel = ncz::flash_fwd_sm100<D, kTma>;
+    const int vidx = (D == 16 ? 0 : D == 32 ? 1 : 2) * 2 + (kTma ? 0 : 1);
+    {
+        std::lock_guard<std::mutex> lock(g_mu);
+        if (dev >= kMaxDevices) return NCZ_ERROR_INVALID_DEVICE;
+        if (!g_attr_done[dev][vidx]) {
+            const cudaError_t e =
+                cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+            if (e != cudaSuccess) return map_cuda_error(e);
+            g_attr_done[dev][vidx] = true;
+        }
+    }
+    kernel<<<grid, ncz::kThreads, L::kAlloc, stream>>>(tq, tk, tv, p);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return map_cuda_error(e);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return NCZ_SUCCESS;
+}
+
+// Validated launch on the current device (the caller switched devices).
+int launch_on_current(const Resolved &r, int dev) {
+    const bool qkv_aligned = aligned(r.q, 16) && aligned(r.k, 16) && aligned(r.v, 16) && r.qs % 8 == 0 &&
+                             r.ks % 8 == 0 && r.vs % 8 == 0 && r.qr % 8 == 0 && r.kr % 8 == 0 && r.vr % 8 == 0;
+    bool use_tma = r.producer == NCZ_PRODUCER_TMA || (r.producer == NCZ_PRODUCER_AUTO && qkv_aligned);
+    if (r.producer == NCZ_PRODUCER_TMA && !qkv_aligned) return NCZ_ERROR_MISALIGNED;
+
+    CUtensorMap tq, tk, tv;
+    std::memset(&tq, 0, sizeof(tq));
+    std::memset(&tk, 0, sizeof(tk));
+    std::memset(&tv, 0, sizeof(tv));
+    if (use_tma) {
+        const bool enc = encode_map(&tq, r.q, r.d, r.seq, r.bh, r.qr, r.qs) &&
+                         encode_map(&tk, r.k, r.d, r.seq, r.bh, r.kr, r.ks) &&
+                         encode_map(&tv, r.v, r.d, r.seq, r.bh, r.vr, r.vs);
+        if (!enc) {
+            if (r.producer == NCZ_PRODUCER_TMA) return NCZ_ERROR_MISALIGNED;
+            use_tma = false;  // e.g. strides the TMA unit cannot express: plain-load producer
+        }
+    }
+
+    FlashParams p;
+    p.q = static_cast<const uint16_t *>(r.q);
+    p.k = static_cast<const uint16_t *>(r.k);
+    p.v = static_cast<const uint16_t *>(r.v);
+    p.o = r.o;
+    p.q_stride = static_cast<long long>(r.qs);
+    p.k_stride = static_cast<long long>(r.ks);
+    p.v_stride = static_cast<long long>(r.vs);
+    p.o_stride = static_cast<long long>(r.os);
+    p.q_row = static_cast<long long>(r.qr);
+    p.k_row = static_cast<long long>(r.kr);
+    p.v_row = static_cast<long long>(r.vr);
+    p.o_row = static_cast<long long>(r.orow);
+    p.seq_len = static_cast<int>(r.seq);
+    p.batch_heads = static_cast<int>(r.bh);
+    p.num_pairs = static_cast<int>((r.seq + 255) / 256);
+    p.scale_log2 = static_cast<float>(static_cast<double>(r.scale) * 1.4426950408889634);
+    p.causal = r.causal != 0;
+    p.o_f16 = r.o_dtype == NCZ_DTYPE_F16;
+    const size_t vec_elems = p.o_f16 ? 8 : 4;
+    p.o_vec = aligned(r.o, 16) && r.os % vec_elems == 0 && r.orow % vec_elems == 0;
+    const unsigned grid = static_cast<unsigned>(static_cast<size_t>(p.num_pairs) * r.bh);
+
+    switch (r.d) {
+        case 16: return use_tma ? launch_variant<16, true>(tq, tk, tv, p, grid, dev, r.stream)
+                                : launch_variant<16, false>(tq, tk, tv, p, grid, dev, r.stream);
+        case 32: return use_tma ? launch_variant<32, true>(tq, tk, tv, p, grid, dev, r.stream)
+                                : launch_variant<32, false>(tq, tk, tv, p, grid, dev, r.stream);
+        default: return use_tma ? launch_variant<64, true>(tq, tk, tv, p, grid, dev, r.stream)
+                                : launch_variant<64, false>(tq, tk, tv, p, grid, dev, r.stream);
+    }
+}
+
+// Switches to r.device when given, launches, restores the caller's device.
+int launch_resolved(const Resolved &r) {
+    int st = validate_resolved(r);
+    if (st != NCZ_SUCCESS) return st;
+    st = ncz_init();
+    if (st != NCZ_SUCCESS) return st;
+    int prev = 0;
+    cudaError_t e = cudaGetDevice(&prev);
+    if (e != cudaSuccess) return map_cuda_error(e);
+    const int dev = r.device >= 0 ? r.device : prev;
+    if (dev != prev) {
+        e = cudaSetDevice(dev);
+        if (e != cudaSuccess) return map_cuda_error(e);
+    }
+    st = launch_on_current(r, dev);
+    if (dev != prev) cudaSetDevice(prev);
+    return st;
+}
+
+Resolved reference_args(const void *q, const void *k, const void *v, void *o, size_t bh, size_t seq, size_t d,
+                        size_t qs, size_t ks, size_t vs, size_t os, float scale, uint32_t causal, void *stream) {
+    ncz_flash_desc desc;
+    std::memset(&desc, 0, sizeof(desc));
+    desc.q = q; desc.k = k; desc.v = v; desc.o = o;
+    desc.batch_heads = bh; desc.seq_len = seq; desc.head_dim = d;
+    desc.q_stride = qs; desc.k_stride = ks; desc.v_stride = vs; desc.o_stride = os;
+    desc.scale = scale; desc.causal = causal;
+    desc.o_dtype = NCZ_DTYPE_F32; desc.producer = NCZ_PRODUCER_AUTO; desc.device = -1;
+    desc.stream = stream;
+    return from_desc(desc);
+}
+
+}  // namespace
+
+extern "C" {
+
+int ncz_init(void) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (g_init_done && g_init_status == NCZ_SUCCESS) return NCZ_SUCCESS;
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess) {
+        g_init_status = map_cuda_error(e);
+        return g_init_status;
+    }
+    if (count <= 0) {
+        g_init_status = NCZ_ERROR_NO_DEVICE;
+        return g_init_status;
+    }
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr) {
+        g_init_status = NCZ_ERROR_NOT_FOUND;
+        return g_init_status;
+    }
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    g_init_done = true;
+    g_init_status = NCZ_SUCCESS;
+    return NCZ_SUCCESS;
+}
+
+int ncz_shutdown(void) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    std::memset(g_attr_done, 0, sizeof(g_attr_done));
+    g_init_done = false;
+    g_init_status = NCZ_ERROR_NOT_INITIALIZED;
+    g_encode = nullptr;
+    return NCZ_SUCCESS;
+}
+
+int ncz_flash_validate(size_t batch_heads, size_t seq_len, size_t head_dim, size_t q_stride, size_t k_stride,
+                       size_t v_stride, size_t o_stride) {
+    // Exactly src/flash.zig:16-28.
+    if (batch_heads == 0 || seq_len == 0) return NCZ_ERROR_INVALID_VALUE;
+    if (head_dim != 16 && head_dim != 32 && head_dim != 64) return NCZ_ERROR_INVALID_VALUE;
+    size_t min_stride;
+    if (!mul_ok(seq_len, head_dim, &min_stride)) return NCZ_ERROR_OVERFLOW;
+    if (q_stride < min_stride || k_stride < min_stride || v_stride < min_stride || o_stride < min_stride)
+        return NCZ_ERROR_INVALID_VALUE;
+    return NCZ_SUCCESS;
+}
+
+int ncz_flash_validate_ex(const ncz_flash_desc *desc) {
+    if (desc == nullptr) return NCZ_ERROR_INVALID_VALUE;
+    return validate_resolved(from_desc(*desc));
+}
+
+int ncz_flash_select(size_t batch_heads, size_t seq_len, size_t head_dim, uint32_t causal, char *label, size_t cap,
+                     uint32_t *threads) {
+    (void)causal;
+    if (batch_heads == 0 || seq_len == 0) return NCZ_ERROR_INVALID_VALUE;
+    if (head_dim != 16 && head_dim != 32 && head_dim != 64) return NCZ_ERROR_INVALID_VALUE;
+    if (label != nullptr && cap > 0) {
+        const char *name = head_dim == 64 ? "flash_fwd_sm100a_d64" : head_dim == 32 ? "flash_fwd_sm100a_d32"
+                                                                                    : "flash_fwd_sm100a_d16";
+        std::strncpy(label, name, cap - 1);
+        label[cap - 1] = '\0';
+    }
+    if (threads != nullptr) *threads = ncz::kThreads;
+    return NCZ_SUCCESS;
+}
+
+int ncz_flash_fwd(const void *q, const void *k, const void *v, void *o, size_t batch_heads, size_t seq_len,
+                  size_t head_dim, size_t q_stride, size_t k_stride, size_t v_stride, size_t o_stride, float scale,
+                  uint32_t causal, void *stream) {
+    const int st = ncz_flash_validate(batch_heads, seq_len, head_dim, q_stride, k_stride, v_stride, o_stride);
+    if (st != NCZ_SUCCESS) return st;
+    return launch_resolved(reference_args(q, k, v, o, batch_heads, seq_len, head_dim, q_stride, k_stride, v_stride,
+                                          o_stride, scale, causal, stream));
+}
+
+int ncz_flash_launch(const void *q, size_t q_len, const void *k, size_t k_len, const void *v, size_t v_len, void *o,
+                     size_t o_len, size_t batch_heads, size_t seq_len, size_t head_dim, size_t q_stride,
+                     size_t k_stride, size_t v_stride, size_t o_stride, float scale, uint32_t causal, void *stream) {
+    int st = ncz_flash_validate(batch_heads, seq_len, head_dim, q_stride, k_stride, v_stride, o_stride);
+    if (st != NCZ_SUCCESS) return st;
+    // requireLen (src/flash.zig:40-43, :98-100): len >= batch_heads * stride.
+    const size_t lens[4] = {q_len, k_len, v_len, o_len};
+    const size_t strides[4] = {q_stride, k_stride, v_stride, o_stride};
+    for (int i = 0; i < 4; ++i) {
+        size_t need;
+        if (!mul_ok(batch_heads, strides[i], &need)) return NCZ_ERROR_OVERFLOW;
+        if (lens[i] < need) return NCZ_ERROR_INVALID_VALUE;
+    }
+    return launch_resolved(reference_args(q, k, v, o, batch_heads, seq_len, head_dim, q_stride, k_stride, v_stride,
+                                          o_stride, scale, causal, stream));
+}
+
+int ncz_flash_fwd_ex(const ncz_flash_desc *desc) {
+    if (desc == nullptr) return NCZ_ERROR_INVALID_VALUE;
+    return launch_resolved(from_desc(*desc));
+}
+
+int ncz_flash_fwd_multi(const ncz_flash_desc *descs, int count) {
+    if (descs == nullptr || count <= 0) return NCZ_ERROR_INVALID_VALUE;
+    for (int i = 0; i < count; ++i) {
+        const int st = validate_resolved(from_desc(descs[i]));
+        if (st != NCZ_SUCCESS) return st;
+    }
+    for (int i = 0; i < count; ++i) {
+        const int st = launch_resolved(from_desc(descs[i]));
+        if (st != NCZ_SUCCESS) return st;
+    }
+    return NCZ_SUCCESS;
+}
+
+int ncz_flash_sync_status(int device, void *stream, uint32_t *detail) {
+    if (detail != nullptr) *detail = 0;
+    int st = ncz_init();
+    if (st != NCZ_SUCCESS) return st;
+    int prev = 0;
+    cudaError_t e = cudaGetDevice(&prev);
+    if (e != cudaSuccess) return map_cuda_error(e);
+    const int dev = device >= 0 ? device : prev;
+    if (dev != prev && (e = cudaSetDevice(dev)) != cudaSuccess) return map_cuda_error(e);
+    uint32_t word = 0;
+    e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&word, ncz::g_ncz_status, sizeof(word));
+    if (e == cudaSuccess && word != 0) {
+        const uint32_t zero = 0;
+        e = cudaMemcpyToSymbol(ncz::g_ncz_status, &zero, sizeof(zero));
+    }
+    if (dev != prev) cudaSetDevice(prev);
+    if (e != cudaSuccess) return map_cuda_error(e);
+    if (detail != nullptr) *detail = word;
+    return word != 0 ? NCZ_ERROR_DEVICE_TIMEOUT : NCZ_SUCCESS;
+}
+
+const char *ncz_status_string(int status) {
+    switch (status) {
+        case NCZ_SUCCESS: return "Success";
+        case NCZ_ERROR_OUT_OF_MEMORY: return "OutOfMemory";
+        case NCZ_ERROR_OVERFLOW: return "Overflow";
+        case NCZ_ERROR_SHARED_OBJECT_INIT_FAILED: return "SharedObjectInitFailed";
+        case NCZ_ERROR_NOT_FOUND: return "NotFound";
+        case NCZ_ERROR_INVALID_VALUE: return "InvalidValue";
+        case NCZ_ERROR_INVALID_CONTEXT: return "InvalidContext";
+        case NCZ_ERROR_INVALID_DEVICE: return "InvalidDevice";
+        case NCZ_ERROR_INVALID_IMAGE: return "InvalidImage";
+        case NCZ_ERROR_CONTEXT_IS_DESTROYED: return "ContextIsDestroyed";
+        case NCZ_ERROR_LAUNCH_FAILED: return "LaunchFailed";
+        case NCZ_ERROR_LAUNCH_OUT_OF_RESOURCES: return "LaunchOutOfResources";
+        case NCZ_ERROR_LAUNCH_TIMEOUT: return "LaunchTimeout";
+        case NCZ_ERROR_ILLEGAL_ADDRESS: return "IllegalAddress";
+        case NCZ_ERROR_NO_DEVICE: return "NoDevice";
+        case NCZ_ERROR_NOT_INITIALIZED: return "NotInitialized";
+        case NCZ_ERROR_UNKNOWN: return "UnknownError";
+        case NCZ_ERROR_DEVICE_TIMEOUT: return "DeviceTimeout";
+        case NCZ_ERROR_MISALIGNED: return "Misaligned";
+        default: return "UnknownStatus";
+    }
+}
+
+uint64_t ncz_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+uint64_t ncz_umma_smem_desc(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes, uint32_t layout_type) {
+    return ncz::umma_smem_desc(smem_addr, lbo_bytes, sbo_bytes, layout_type);
+}
+
+uint32_t ncz_umma_instr_desc_f16(uint32_t m, uint32_t n, uint32_t a_major, uint32_t b_major) {
+    return ncz::umma_idesc_f16_f32(m, n, a_major, b_major);
+}
+
+uint32_t ncz_tma_swizzle_offset(uint32_t span_bytes, uint32_t offset) {
+    if (span_bytes != 32 && span_bytes != 64 && span_bytes != 128) return offset;
+    return ncz::tma_swizzle(span_bytes, offset);
+}
+
+}  // extern "C"

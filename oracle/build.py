@@ -1,0 +1,61 @@
+"""Build recipes for the test oracle (TEST INFRASTRUCTURE ONLY).
+
+- liboracle.so: the plain-C restatement of the reference CPU attention
+  (oracle/flash_oracle.c), gcc -O2 -fno-fast-math -fopenmp.
+- _ref/libncz_ref.so and _ref/cuda_baselines: the reference's own
+  tools/cuda_baselines.cu compiled from where it lies in the reference tree
+  (only when that tree is present); they travel to GPU boxes as built files.
+"""
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ORACLE_SO = os.path.join(HERE, "liboracle.so")
+REF_DIR = os.path.join(HERE, "_ref")
+REF_SO = os.path.join(REF_DIR, "libncz_ref.so")
+REF_BIN = os.path.join(REF_DIR, "cuda_baselines")
+REFERENCE_ROOT = os.environ.get("NCZ_REFERENCE_ROOT", "/root/reference")
+NVCC = os.environ.get("NVCC", "nvcc")
+
+
+def _run(cmd):
+    subprocess.run(cmd, check=True)
+
+
+def _stale(out, srcs):
+    if not os.path.exists(out):
+        return True
+    t = os.path.getmtime(out)
+    return any(os.path.getmtime(s) > t for s in srcs)
+
+
+def build_oracle(force: bool = False) -> str:
+    src = os.path.join(HERE, "flash_oracle.c")
+    if force or _stale(ORACLE_SO, [src]):
+        _run(["gcc", "-O2", "-fno-fast-math", "-fopenmp", "-fPIC", "-shared", "-std=c11", src, "-o", ORACLE_SO,
+              "-lm"])
+    return ORACLE_SO
+
+
+def build_reference(force: bool = False) -> bool:
+    """Builds oracle/_ref from the reference sources; False when they are absent."""
+    tools = os.path.join(REFERENCE_ROOT, "tools")
+    src = os.path.join(tools, "cuda_baselines.cu")
+    if not os.path.exists(src) or shutil.which(NVCC) is None:
+        return False
+    os.makedirs(REF_DIR, exist_ok=True)
+    harness = os.path.join(HERE, "ref_harness.cu")
+    if force or _stale(REF_SO, [src, harness]):
+        _run([NVCC, "-O3", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a", "-Xcompiler", "-fPIC",
+              "-shared", "-Dmain=ncz_reference_baselines_main", "-I", tools, harness, "-lcublas", "-o", REF_SO])
+    if force or _stale(REF_BIN, [src]):
+        _run([NVCC, "-O3", "-std=c++17", "-arch=sm_100a", src, "-lcublas", "-o", REF_BIN])
+    return True
+
+
+if __name__ == "__main__":
+    print(build_oracle(force=True))
+    print("reference built:", build_reference(force=True))

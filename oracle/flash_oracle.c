@@ -1,0 +1,180 @@
+/*
+ * CPU oracle for the flash-attention forward path -- TEST INFRASTRUCTURE ONLY.
+ *
+ * This file is the parity checker for the sm_100a kernel in
+ * not-cute-zig_b200/csrc.  Only tests/, __graft_entry__.smoke() and bench.py's
+ * CPU-baseline leg load it.  The product library never links or calls it.
+ *
+ * It restates, in plain C, the reference's CPU attention:
+ *   - computeFlashReferenceOne    src/main.zig:1271-1307
+ *   - computeFlashReferenceSlices src/main.zig:1242-1269
+ *   - fillFlashInput              src/main.zig:1207-1211
+ *   - the benchmark input pattern src/main.zig:782-791 (mod 11 / 13 / 17)
+ * The operation order is kept: an f32 dot product in ascending k, then
+ * `score *= scale`; -inf for future keys under causal masking; a running row
+ * max; weights exp(score - max) summed in ascending key order; then, for each
+ * output column, acc += (weight / row_sum) * v in ascending key order.
+ *
+ * Extension (not expressible in the reference API): per-row element strides
+ * for Q/K/V/O.  With row_stride == head_dim this is exactly the reference.
+ *
+ * Also here: a seeded generator (splitmix64 -> uniform -> Box-Muller), so
+ * synthetic inputs are bit-identical on every machine.  The kernel and the
+ * oracle both read the same f16 bits.
+ *
+ * Build: gcc -O2 -fno-fast-math -fopenmp -shared -fPIC (see oracle/build.py).
+ */
+#include <math.h>
+#include <stddef.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+typedef uint16_t f16bits;
+
+static inline float h2f(f16bits h) {
+    _Float16 v;
+    memcpy(&v, &h, 2);
+    return (float)v;
+}
+
+static inline f16bits f2h(float f) {
+    _Float16 v = (_Float16)f; /* round to nearest even */
+    f16bits h;
+    memcpy(&h, &v, 2);
+    return h;
+}
+
+/* Restates computeFlashReferenceOne (src/main.zig:1271-1307) for one
+ * batch x head slice; `scores` is caller-provided scratch of seq_len floats. */
+static void flash_one_row(size_t seq_len, size_t head_dim, size_t row, const f16bits *q,
+                          size_t q_row, const f16bits *k, size_t k_row, const f16bits *v,
+                          size_t v_row, float *o, size_t o_row, float scale, uint32_t causal,
+                          float *scores) {
+    float row_max = -INFINITY;
+    for (size_t key = 0; key < seq_len; ++key) {
+        if (causal != 0 && key > row) {
+            scores[key] = -INFINITY; /* main.zig:1277-1278 */
+        } else {
+            float score = 0.0f;
+            for (size_t kk = 0; kk < head_dim; ++kk) /* main.zig:1281-1284 */
+                score += h2f(q[row * q_row + kk]) * h2f(k[key * k_row + kk]);
+            score *= scale; /* main.zig:1285 */
+            scores[key] = score;
+            row_max = fmaxf(row_max, score);
+        }
+    }
+    float row_sum = 0.0f;
+    for (size_t key = 0; key < seq_len; ++key) { /* main.zig:1291-1296 */
+        const float weight = scores[key] == -INFINITY ? 0.0f : expf(scores[key] - row_max);
+        scores[key] = weight;
+        row_sum += weight;
+    }
+    for (size_t col = 0; col < head_dim; ++col) { /* main.zig:1298-1305 */
+        float acc = 0.0f;
+        for (size_t key = 0; key < seq_len; ++key) {
+            const float weight = scores[key] / row_sum;
+            acc += weight * h2f(v[key * v_row + col]);
+        }
+        o[row * o_row + col] = acc;
+    }
+}
+
+/*
+ * All slices (computeFlashReferenceSlices, src/main.zig:1242-1269) with the
+ * row-stride extension.  Slices and rows are independent, so (slice, row)
+ * pairs are spread over `nthreads` OpenMP threads (<= 0: all available).
+ * Rows `row_begin..row_end` of every slice are computed (the full range is
+ * 0..seq_len); the CPU baseline uses a subrange as its bounded sample.
+ * Output elements outside the active rows are not touched.
+ */
+void ncz_oracle_flash(size_t batch_heads, size_t seq_len, size_t head_dim, const f16bits *q,
+                      size_t q_stride, size_t q_row, const f16bits *k, size_t k_stride,
+                      size_t k_row, const f16bits *v, size_t v_stride, size_t v_row, float *o,
+                      size_t o_stride, size_t o_row, float scale, uint32_t causal,
+                      size_t row_begin, size_t row_end, int nthreads) {
+    if (row_end > seq_len) row_end = seq_len;
+    if (row_begin >= row_end || batch_heads == 0) return;
+    const size_t rows = row_end - row_begin;
+    const long long total = (long long)(batch_heads * rows);
+#ifdef _OPENMP
+    if (nthreads <= 0) nthreads = omp_get_max_threads();
+#else
+    (void)nthreads;
+#endif
+#pragma omp parallel num_threads(nthreads)
+    {
+        float *scores = (float *)malloc(seq_len * sizeof(float));
+#pragma omp for schedule(dynamic, 4)
+        for (long long i = 0; i < total; ++i) {
+            const size_t slice = (size_t)i / rows;
+            const size_t row = row_begin + (size_t)i % rows;
+            flash_one_row(seq_len, head_dim, row, q + slice * q_stride, q_row,
+                          k + slice * k_stride, k_row, v + slice * v_stride, v_row,
+                          o + slice * o_stride, o_row, scale, causal, scores);
+        }
+        free(scores);
+    }
+}
+
+/* fillFlashInput (src/main.zig:1207-1211):
+ * data[i] = f16(((i * mul + add) % modulus) * scale); the smoke and compare
+ * inputs use modulus 17, the benchmark inputs use 11 / 13 / 17 (main.zig:782-791). */
+void ncz_oracle_fill_pattern(f16bits *data, size_t n, size_t mul, size_t add, size_t modulus,
+                             float scale) {
+    for (size_t i = 0; i < n; ++i)
+        data[i] = f2h((float)((i * mul + add) % modulus) * scale);
+}
+
+static inline uint64_t splitmix64(uint64_t *state) {
+    uint64_t z = (*state += 0x9E3779B97F4A7C15ull);
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+/* Uniform double in (0, 1): 53 random bits, offset by half an ulp so 0 never occurs. */
+static inline double uniform01(uint64_t *state) {
+    return ((double)(splitmix64(state) >> 11) + 0.5) * (1.0 / 9007199254740992.0);
+}
+
+/* f16(mean + std * N(0,1)); Box-Muller on pairs from splitmix64(seed). */
+void ncz_oracle_fill_normal(f16bits *data, size_t n, uint64_t seed, float mean, float stddev) {
+    uint64_t state = seed;
+    const double two_pi = 6.283185307179586476925286766559;
+    for (size_t i = 0; i < n; i += 2) {
+        const double u1 = uniform01(&state), u2 = uniform01(&state);
+        const double r = sqrt(-2.0 * log(u1));
+        data[i] = f2h((float)(mean + stddev * r * cos(two_pi * u2)));
+        if (i + 1 < n) data[i + 1] = f2h((float)(mean + stddev * r * sin(two_pi * u2)));
+    }
+}
+
+/* f16(U(lo, hi)) from splitmix64(seed). */
+void ncz_oracle_fill_uniform(f16bits *data, size_t n, uint64_t seed, float lo, float hi) {
+    uint64_t state = seed;
+    for (size_t i = 0; i < n; ++i) data[i] = f2h((float)(lo + (hi - lo) * uniform01(&state)));
+}
+
+/* Sets every element of a strided [batch_heads, seq_len, row] view whose
+ * column is >= head_dim (the row padding) to `value_bits` (e.g. an f16 NaN).
+ * Padding only exists when row_stride > head_dim. */
+void ncz_oracle_fill_row_padding(f16bits *data, size_t batch_heads, size_t seq_len,
+                                 size_t head_dim, size_t slice_stride, size_t row_stride,
+                                 f16bits value_bits) {
+    for (size_t b = 0; b < batch_heads; ++b)
+        for (size_t r = 0; r < seq_len; ++r)
+            for (size_t c = head_dim; c < row_stride; ++c)
+                data[b * slice_stride + r * row_stride + c] = value_bits;
+}
+
+int ncz_oracle_max_threads(void) {
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}

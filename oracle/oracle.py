@@ -1,0 +1,99 @@
+"""numpy front end of the C oracle (flash_oracle.c) -- TEST INFRASTRUCTURE ONLY.
+
+Restates the reference CPU attention computeFlashReferenceOne
+(src/main.zig:1271-1307) and its input generator fillFlashInput
+(src/main.zig:1207-1211); see flash_oracle.c for the line-by-line mapping.
+f16 arrays are numpy float16; outputs are float32.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+from . import build as _build
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_build.ORACLE_SO):
+            _build.build_oracle()
+        h = ctypes.CDLL(_build.ORACLE_SO)
+        sz, vp = ctypes.c_size_t, ctypes.c_void_p
+        h.ncz_oracle_flash.restype = None
+        h.ncz_oracle_flash.argtypes = [sz, sz, sz, vp, sz, sz, vp, sz, sz, vp, sz, sz, vp, sz, sz,
+                                       ctypes.c_float, ctypes.c_uint32, sz, sz, ctypes.c_int]
+        h.ncz_oracle_fill_pattern.restype = None
+        h.ncz_oracle_fill_pattern.argtypes = [vp, sz, sz, sz, sz, ctypes.c_float]
+        h.ncz_oracle_fill_normal.restype = None
+        h.ncz_oracle_fill_normal.argtypes = [vp, sz, ctypes.c_uint64, ctypes.c_float, ctypes.c_float]
+        h.ncz_oracle_fill_uniform.restype = None
+        h.ncz_oracle_fill_uniform.argtypes = [vp, sz, ctypes.c_uint64, ctypes.c_float, ctypes.c_float]
+        h.ncz_oracle_fill_row_padding.restype = None
+        h.ncz_oracle_fill_row_padding.argtypes = [vp, sz, sz, sz, sz, sz, ctypes.c_uint16]
+        h.ncz_oracle_max_threads.restype = ctypes.c_int
+        h.ncz_oracle_max_threads.argtypes = []
+        _lib = h
+    return _lib
+
+
+def _ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+def fill_pattern(n: int, mul: int, add: int, scale: float, modulus: int = 17) -> np.ndarray:
+    """fillFlashInput (src/main.zig:1207-1211): f16(((i*mul+add) % modulus) * scale)."""
+    out = np.empty(n, dtype=np.float16)
+    lib().ncz_oracle_fill_pattern(_ptr(out), n, mul, add, modulus, scale)
+    return out
+
+
+def fill_normal(n: int, seed: int, mean: float = 0.0, std: float = 1.0) -> np.ndarray:
+    """f16(mean + std * N(0,1)) from splitmix64(seed) + Box-Muller."""
+    out = np.empty(n, dtype=np.float16)
+    lib().ncz_oracle_fill_normal(_ptr(out), n, seed, mean, std)
+    return out
+
+
+def fill_uniform(n: int, seed: int, lo: float = -1.0, hi: float = 1.0) -> np.ndarray:
+    """f16(U(lo, hi)) from splitmix64(seed)."""
+    out = np.empty(n, dtype=np.float16)
+    lib().ncz_oracle_fill_uniform(_ptr(out), n, seed, lo, hi)
+    return out
+
+
+def fill_row_padding(a: np.ndarray, batch_heads: int, seq_len: int, head_dim: int, slice_stride: int,
+                     row_stride: int, value=np.float16(np.nan)) -> None:
+    """Writes `value` into every padding element (column >= head_dim) of a strided view."""
+    bits = np.array([value], dtype=np.float16).view(np.uint16)[0]
+    lib().ncz_oracle_fill_row_padding(_ptr(a), batch_heads, seq_len, head_dim, slice_stride, row_stride,
+                                      int(bits))
+
+
+def flash_reference(q: np.ndarray, k: np.ndarray, v: np.ndarray, *, batch_heads: int, seq_len: int,
+                    head_dim: int, q_stride: int, k_stride: int, v_stride: int, o_stride: int,
+                    scale: float, causal: bool, row_strides=None, out: np.ndarray | None = None,
+                    rows: tuple[int, int] | None = None, threads: int = 0) -> np.ndarray:
+    """The reference CPU attention over all slices (computeFlashReferenceSlices,
+    src/main.zig:1242-1269), with optional per-row strides (default head_dim).
+
+    Returns a float32 array of batch_heads * o_stride elements (unwritten
+    elements are 0, as the reference's `expected` buffer is zero-filled)."""
+    qr, kr, vr, orow = row_strides if row_strides is not None else (head_dim,) * 4
+    for a in (q, k, v):
+        assert a.dtype == np.float16 and a.flags.c_contiguous
+    if out is None:
+        out = np.zeros(batch_heads * o_stride, dtype=np.float32)
+    r0, r1 = rows if rows is not None else (0, seq_len)
+    lib().ncz_oracle_flash(batch_heads, seq_len, head_dim, _ptr(q), q_stride, qr, _ptr(k), k_stride, kr,
+                           _ptr(v), v_stride, vr, _ptr(out), o_stride, orow, float(scale), int(bool(causal)),
+                           r0, r1, threads)
+    return out
+
+
+def max_threads() -> int:
+    return int(lib().ncz_oracle_max_threads())

@@ -1,0 +1,196 @@
+"""Parity of the sm_100a kernel with the oracle, through the C ABI.
+
+Every launch goes through the reference-shaped Python mirror
+(not-cute-zig_b200.flash.launch / launch_ex -> libncz_flash.so).  Inputs are
+generated on the host, so the kernel and the oracle read identical f16 bits.
+"""
+import math
+
+import numpy as np
+import pytest
+
+from tests import cases as C
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+if not torch.cuda.is_available():
+    pytest.skip("no CUDA device", allow_module_level=True)
+
+SENTINEL = 12345.0
+
+
+def run(ncz, p: C.Problem, *, o_dtype="float32", producer="auto", via="auto"):
+    dev = torch.device("cuda:0")
+    q = torch.from_numpy(p.q).to(dev)
+    k = torch.from_numpy(p.k).to(dev)
+    v = torch.from_numpy(p.v).to(dev)
+    o = torch.full((p.bh * p.strides[3],), SENTINEL, dtype=getattr(torch, o_dtype), device=dev)
+    opts = ncz.Options(seq_len=p.seq, head_dim=p.d, q_stride=p.strides[0], k_stride=p.strides[1],
+                       v_stride=p.strides[2], o_stride=p.strides[3], scale=p.scale, batch_heads=p.bh,
+                       causal=p.causal)
+    plain = p.row_strides is None and o_dtype == "float32" and producer == "auto"
+    if via == "launch" or (via == "auto" and plain):
+        ncz.launch(q, k, v, o, opts)
+    else:
+        ncz.launch_ex(q, k, v, o, opts, row_strides=p.row_strides, producer=producer)
+    assert ncz.sync_status() == 0
+    return o.float().cpu().numpy()
+
+
+def untouched(got, p, idx):
+    mask = np.ones(got.size, dtype=bool)
+    mask[idx] = False
+    return bool(np.all(got[mask] == SENTINEL))
+
+
+@pytest.mark.parametrize("case", C.SMOKE_CASES, ids=lambda c: f"bh{c[0]}_s{c[1]}_d{c[2]}_c{int(c[4])}")
+def test_reference_smoke_cases(ncz, oracle_mod, case):
+    """src/main.zig:189-287: odd slice strides (LSU producer), 0.008 there, 2e-3 here."""
+    bh, s, d, strides, causal = case
+    p = C.pattern_problem(bh, s, d, strides, causal, oracle_mod)
+    got = run(ncz, p)
+    want = C.reference(p, oracle_mod)
+    idx = C.active_index(p)
+    C.check(got, want, idx, f"smoke {case}")
+    assert untouched(got, p, idx), "kernel wrote outside the active rows"
+
+
+@pytest.mark.parametrize("case", C.COMPARE_CASES, ids=lambda c: f"bh{c[0]}_s{c[1]}_d{c[2]}_c{int(c[3])}")
+def test_reference_compare_cases(ncz, oracle_mod, case):
+    """src/main.zig:141-170 shapes with fillFlashInput data (0.02 there, 2e-3 here)."""
+    bh, s, d, causal = case
+    p = C.pattern_problem(bh, s, d, (s * d,) * 4, causal, oracle_mod)
+    got = run(ncz, p)
+    C.check(got, C.reference(p, oracle_mod), C.active_index(p), f"compare {case}")
+
+
+def test_config1_smoke(ncz, oracle_mod):
+    """bh=2, S=64, d=32, causal, N(0, 0.5^2) seed 0, O f32."""
+    p = C.normal_problem(2, 64, 32, True, 0, oracle_mod, std=0.5)
+    got = run(ncz, p)
+    C.check(got, C.reference(p, oracle_mod), C.active_index(p), "config1")
+
+
+def test_config2_profile_f16_out(ncz, oracle_mod):
+    """bh=8, S=1024, d=64, causal, N(0, 0.5^2) seed 1, f16 O."""
+    p = C.normal_problem(8, 1024, 64, True, 1, oracle_mod, std=0.5)
+    got = run(ncz, p, o_dtype="float16")
+    want = C.reference(p, oracle_mod)
+    idx = C.active_index(p)
+    err = np.abs(got[idx].astype(np.float64) - want[idx])
+    # f16 output adds at most half an f16 ulp of |O| on top of the f32 tolerance.
+    assert np.all(err <= C.ATOL + np.abs(want[idx]) * 2.0 ** -11), err.max()
+
+
+def test_config3_padded_rows_nan_pad(ncz, oracle_mod):
+    """bh=512, S=128, d=32, row stride 40 with NaN padding,
+    slice stride 128*40, U(-1,1) seed 2, non-causal.  NaN over-reads would poison O."""
+    bh, s, d, rs = 512, 128, 32, 40
+    st = s * rs
+    p = C.Problem(bh, s, d, (st, st, st, s * d), False, 1.0 / math.sqrt(d), row_strides=(rs, rs, rs, d))
+    p.q = oracle_mod.fill_uniform(bh * st, 6, -1.0, 1.0)
+    p.k = oracle_mod.fill_uniform(bh * st, 7, -1.0, 1.0)
+    p.v = oracle_mod.fill_uniform(bh * st, 8, -1.0, 1.0)
+    for a in (p.q, p.k, p.v):
+        oracle_mod.fill_row_padding(a, bh, s, d, st, rs)
+    got = run(ncz, p)
+    C.check(got, C.reference(p, oracle_mod), C.active_index(p), "config3")
+
+
+def test_config4_long_causal_sampled(ncz, oracle_mod):
+    """bh=64, S=8192, d=64, causal, N(0,1), K x2 (peaked rows).
+    The oracle runs on slices {0, 63} (all rows) and a row band of slice 31;
+    all slices are checked for finiteness and the convex-hull property."""
+    p = C.normal_problem(64, 8192, 64, True, 3, oracle_mod, std=1.0, k_mul=2.0)
+    got = run(ncz, p)
+    want = C.reference(p, oracle_mod, slices=[0, 63])
+    C.check(got, want, C.active_index(p, slices=[0, 63]), "config4 slices 0,63")
+    band = C.reference(p, oracle_mod, slices=[31], rows=(4000, 4200))
+    C.check(got, band, C.active_index(p, slices=[31], rows=(4000, 4200)), "config4 slice 31 band")
+    o = got.reshape(64, 8192, 64)
+    v = p.v.astype(np.float32).reshape(64, 8192, 64)
+    assert np.all(np.isfinite(o))
+    # O is a convex combination of V rows up to P's f16 rounding (relative 2^-11 per weight).
+    slack = 2.0 ** -11 * float(np.abs(v).max()) + 1e-4
+    assert np.all(o <= v.max(axis=1, keepdims=True) + slack) and np.all(o >= v.min(axis=1, keepdims=True) - slack)
+
+
+@pytest.mark.parametrize("d,seed", [(64, 4), (16, 5)])
+def test_config5_sweep_sampled(ncz, oracle_mod, d, seed):
+    """bh=1024, S=2048, non-causal, N(0, 0.5^2); oracle on 3 slices."""
+    p = C.normal_problem(1024, 2048, d, False, seed, oracle_mod, std=0.5)
+    got = run(ncz, p)
+    sl = [0, 517, 1023]
+    C.check(got, C.reference(p, oracle_mod, slices=sl), C.active_index(p, slices=sl), f"config5 d{d}")
+    assert np.all(np.isfinite(got))
+
+
+SEQS = [1, 2, 15, 16, 17, 127, 128, 129, 255, 256, 257, 383, 385, 512, 640, 1000]
+
+
+@pytest.mark.parametrize("d", [16, 32, 64])
+@pytest.mark.parametrize("causal", [False, True])
+def test_sequence_residues(ncz, oracle_mod, d, causal):
+    """Residue tiles, single-row sequences, odd Q-tile pairs, diagonal tiles."""
+    for s in SEQS:
+        p = C.normal_problem(3, s, d, causal, 100 + s, oracle_mod, std=0.7)
+        got = run(ncz, p)
+        C.check(got, C.reference(p, oracle_mod), C.active_index(p), f"S={s} d={d} causal={causal}")
+
+
+@pytest.mark.parametrize("d", [16, 32, 64])
+def test_tma_and_lsu_producers_agree(ncz, oracle_mod, d):
+    """Both producers fill identical swizzled tiles, so outputs are bit-identical."""
+    p = C.normal_problem(5, 300, d, True, 7, oracle_mod, std=0.6)
+    a = run(ncz, p, producer="tma")
+    b = run(ncz, p, producer="lsu")
+    C.check(a, C.reference(p, oracle_mod), C.active_index(p), "tma")
+    assert np.array_equal(a, b)
+
+
+@pytest.mark.parametrize("scale", [-0.125, 0.0, 2.0])
+def test_scale_edge_cases(ncz, oracle_mod, scale):
+    """Non-positive scales take the scale-then-mask path; a large scale peaks rows."""
+    p = C.normal_problem(2, 200, 32, True, 9, oracle_mod, std=0.5, scale=scale)
+    C.check(run(ncz, p), C.reference(p, oracle_mod), C.active_index(p), f"scale={scale}")
+
+
+def test_multi_descriptor_launch(ncz, oracle_mod):
+    """ncz_flash_fwd_multi: two slice shards (on device 0) in one call."""
+    p = C.normal_problem(6, 333, 64, False, 11, oracle_mod)
+    dev = torch.device("cuda:0")
+    n = 333 * 64
+    q, k, v = (torch.from_numpy(a).to(dev) for a in (p.q, p.k, p.v))
+    o = torch.full((6 * n,), SENTINEL, dtype=torch.float32, device=dev)
+    descs = []
+    for lo, hi in ((0, 4), (4, 6)):
+        opts = ncz.Options(seq_len=333, head_dim=64, q_stride=n, k_stride=n, v_stride=n, o_stride=n,
+                           scale=p.scale, batch_heads=hi - lo)
+        descs.append(ncz.flash.make_desc(q[lo * n:hi * n], k[lo * n:hi * n], v[lo * n:hi * n], o[lo * n:hi * n],
+                                         opts, device=0))
+    ncz.launch_multi(descs)
+    assert ncz.sync_status() == 0
+    C.check(o.cpu().numpy(), C.reference(p, oracle_mod), C.active_index(p), "multi")
+
+
+def test_invalid_arguments_raise_before_launch(ncz):
+    dev = torch.device("cuda:0")
+    t = torch.zeros(64 * 16, dtype=torch.float16, device=dev)
+    o = torch.zeros(64 * 16, dtype=torch.float32, device=dev)
+    before = ncz.flash.launch_count()
+    bad = [
+        dict(seq_len=64, head_dim=48, q_stride=64 * 48, k_stride=64 * 48, v_stride=64 * 48, o_stride=64 * 48),
+        dict(seq_len=0, head_dim=16, q_stride=0, k_stride=0, v_stride=0, o_stride=0),
+        dict(seq_len=64, head_dim=16, q_stride=64 * 16 - 1, k_stride=1024, v_stride=1024, o_stride=1024),
+        dict(seq_len=64, head_dim=16, q_stride=1024, k_stride=1024, v_stride=1024, o_stride=1024, batch_heads=2),
+    ]
+    for kw in bad:
+        with pytest.raises(ncz.FlashError) as e:
+            ncz.launch(t, t, t, o, ncz.Options(scale=0.25, **kw))
+        assert e.value.name == "InvalidValue"
+    assert ncz.flash.launch_count() == before
+
+
+def test_status_word_clean(ncz):
+    assert ncz.sync_status() == 0
