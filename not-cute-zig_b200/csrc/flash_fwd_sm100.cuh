@@ -11,8 +11,9 @@
 // a STAGES-deep ring of 128-key tiles shared by both Q tiles.
 //
 // Warp roles (384 threads):
-//   warp 0      producer: TMA (one lane) or LSU (all lanes) loads of Q, K, V
-//   warp 1      TMEM allocator + tcgen05 MMA issuer (one lane)
+//   warp 0      producer: TMA or LSU loads of Q, K, V
+//   warp 1      TMEM allocator + tcgen05 MMA issuer
+//   (both run as whole warps; elect.sync picks the lane that issues)
 //   warps 2,3   idle (keep the softmax warpgroups warpgroup-aligned)
 //   warps 4-7   softmax for Q tile 0 (thread = row = TMEM lane)
 //   warps 8-11  softmax for Q tile 1
@@ -62,6 +63,7 @@ enum WaitSite : uint32_t {
     kSiteODone = 8,
     kSiteMmaDrain = 9,
     kSiteProducerDrain = 10,
+    kSiteTurn = 11,
 };
 
 struct FlashParams {
@@ -91,6 +93,7 @@ struct SmemLayout {
     static constexpr int kOffV = kOffK + kStages * kTile;
     static constexpr int kOffBar = kOffV + kStages * kTile;
     // barriers: q_full | k_full[S] | v_full[S] | kv_empty[S] | s_full[2] | s_free[2] | p_full[2] | o_done[2] | drain
+    //           | turn[2]
     static constexpr int kBarQFull = 0;
     static constexpr int kBarKFull = 1;
     static constexpr int kBarVFull = kBarKFull + kStages;
@@ -100,7 +103,8 @@ struct SmemLayout {
     static constexpr int kBarPFull = kBarSFree + 2;
     static constexpr int kBarODone = kBarPFull + 2;
     static constexpr int kBarDrain = kBarODone + 2;
-    static constexpr int kNumBars = kBarDrain + 1;
+    static constexpr int kBarTurn = kBarDrain + 1;  // exp-phase hand-off between the softmax warpgroups
+    static constexpr int kNumBars = kBarTurn + 2;
     static constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
     static constexpr int kOffAbort = kOffTmemSlot + 4;
     static constexpr int kBytes = kOffAbort + 4;
@@ -177,10 +181,11 @@ struct Bars {
     __device__ __forceinline__ uint32_t p_full(int w) const { return at(L::kBarPFull + w); }
     __device__ __forceinline__ uint32_t o_done(int w) const { return at(L::kBarODone + w); }
     __device__ __forceinline__ uint32_t drain() const { return at(L::kBarDrain); }
+    __device__ __forceinline__ uint32_t turn(int w) const { return at(L::kBarTurn + w); }
 };
 
 // ---------------------------------------------------------------------------
-// producer, TMA variant (one lane)
+// producer, TMA variant (whole warp; elect.sync picks the issuing lane)
 // ---------------------------------------------------------------------------
 template <int D>
 __device__ __forceinline__ void producer_tma(const CUtensorMap *tq, const CUtensorMap *tk,
@@ -191,21 +196,20 @@ __device__ __forceinline__ void producer_tma(const CUtensorMap *tq, const CUtens
     uint32_t qbytes = 0;
 #pragma unroll
     for (int w = 0; w < kQTiles; ++w) qbytes += wk.n[w] > 0 ? L::kTile : 0;
-    mbar_arrive_expect_tx(b.q_full(), qbytes);
+    mbar_arrive_expect_tx_elect(b.q_full(), qbytes);
 #pragma unroll
     for (int w = 0; w < kQTiles; ++w)
         if (wk.n[w] > 0)
-            tma_load_3d(sbase + L::kOffQ + w * L::kTile, tq, b.q_full(), 0, wk.q_base + w * kBlockM, wk.slice);
+            tma_load_3d_elect(sbase + L::kOffQ + w * L::kTile, tq, b.q_full(), 0, wk.q_base + w * kBlockM, wk.slice);
     int j = 0;
     for (; j < wk.n_max; ++j) {
         const int st = j % L::kStages;
-        if (j >= L::kStages &&
-            !bounded_wait(b.kv_empty(st), ((j / L::kStages) - 1) & 1, abort_flag, kSiteKvEmpty, true))
+        if (j >= L::kStages && !warp_wait(b.kv_empty(st), ((j / L::kStages) - 1) & 1, abort_flag, kSiteKvEmpty))
             break;
-        mbar_arrive_expect_tx(b.k_full(st), L::kTile);
-        tma_load_3d(sbase + L::kOffK + st * L::kTile, tk, b.k_full(st), 0, j * kBlockN, wk.slice);
-        mbar_arrive_expect_tx(b.v_full(st), L::kTile);
-        tma_load_3d(sbase + L::kOffV + st * L::kTile, tv, b.v_full(st), 0, j * kBlockN, wk.slice);
+        mbar_arrive_expect_tx_elect(b.k_full(st), L::kTile);
+        tma_load_3d_elect(sbase + L::kOffK + st * L::kTile, tk, b.k_full(st), 0, j * kBlockN, wk.slice);
+        mbar_arrive_expect_tx_elect(b.v_full(st), L::kTile);
+        tma_load_3d_elect(sbase + L::kOffV + st * L::kTile, tv, b.v_full(st), 0, j * kBlockN, wk.slice);
     }
     // Every issued copy must land before shared memory is released.
     bounded_wait(b.q_full(), 0, abort_flag, kSiteProducerDrain, false);
@@ -215,6 +219,7 @@ __device__ __forceinline__ void producer_tma(const CUtensorMap *tq, const CUtens
         bounded_wait(b.k_full(st), ph, abort_flag, kSiteProducerDrain, false);
         bounded_wait(b.v_full(st), ph, abort_flag, kSiteProducerDrain, false);
     }
+    __syncwarp();
 }
 
 // ---------------------------------------------------------------------------
@@ -272,14 +277,14 @@ __device__ __forceinline__ void producer_lsu(const FlashParams &p, uint8_t *smem
 }
 
 // ---------------------------------------------------------------------------
-// MMA issuer (one lane)
+// MMA issuer (whole warp; elect.sync picks the issuing lane)
 // ---------------------------------------------------------------------------
 template <int D>
 __device__ __forceinline__ bool issue_pv(int t, const Bars<D> &b, uint32_t sbase, uint32_t tmem, const Work &wk,
                                          volatile uint32_t *abort_flag) {
     using L = SmemLayout<D>;
     const int st = t % L::kStages;
-    if (!bounded_wait(b.v_full(st), (t / L::kStages) & 1, abort_flag, kSiteVFull, true)) return false;
+    if (!warp_wait(b.v_full(st), (t / L::kStages) & 1, abort_flag, kSiteVFull)) return false;
     tc_fence_after();
     constexpr uint32_t idesc_pv = umma_idesc_f16_f32(kBlockM, D, 0, 1);  // B = V, MN-major
     // V tile: 128 keys x D, rows of 2D bytes (one swizzle atom wide); 8-row groups 8*span apart.
@@ -287,17 +292,17 @@ __device__ __forceinline__ bool issue_pv(int t, const Bars<D> &b, uint32_t sbase
 #pragma unroll
     for (int w = 0; w < kQTiles; ++w) {
         if (t < wk.n[w]) {
-            if (!bounded_wait(b.p_full(w), t & 1, abort_flag, kSitePFull, true)) return false;
+            if (!warp_wait(b.p_full(w), t & 1, abort_flag, kSitePFull)) return false;
             tc_fence_after();
             const uint32_t tP = tmem + w * 256 + 128, tO = tmem + w * 256 + 192;
 #pragma unroll
             for (int kk = 0; kk < kBlockN / 16; ++kk)
-                umma_ts(tO, tP + kk * 8, vdesc + static_cast<uint64_t>((kk * 16 * L::kSpan) >> 4), idesc_pv,
-                        (t > 0 || kk > 0) ? 1u : 0u);
-            umma_commit(b.o_done(w));
+                umma_ts_elect(tO, tP + kk * 8, vdesc + static_cast<uint64_t>((kk * 16 * L::kSpan) >> 4), idesc_pv,
+                              (t > 0 || kk > 0) ? 1u : 0u);
+            umma_commit_elect(b.o_done(w));
         }
     }
-    umma_commit(b.kv_empty(st));
+    umma_commit_elect(b.kv_empty(st));
     return true;
 }
 
@@ -306,11 +311,11 @@ __device__ __forceinline__ void mma_role(uint32_t sbase, uint32_t tmem, const Wo
     using L = SmemLayout<D>;
     const Bars<D> b{sbase};
     constexpr uint32_t idesc_qk = umma_idesc_f16_f32(kBlockM, kBlockN, 0, 0);  // both K-major
-    bool ok = bounded_wait(b.q_full(), 0, abort_flag, kSiteQFull, true);
+    bool ok = warp_wait(b.q_full(), 0, abort_flag, kSiteQFull);
     if (ok) tc_fence_after();
     for (int j = 0; ok && j < wk.n_max; ++j) {
         const int st = j % L::kStages;
-        ok = bounded_wait(b.k_full(st), (j / L::kStages) & 1, abort_flag, kSiteKFull, true);
+        ok = warp_wait(b.k_full(st), (j / L::kStages) & 1, abort_flag, kSiteKFull);
         if (!ok) break;
         tc_fence_after();
         const uint64_t kdesc = umma_smem_desc(sbase + L::kOffK + st * L::kTile, 16, 8 * L::kSpan, L::kUmmaLayout);
@@ -318,7 +323,7 @@ __device__ __forceinline__ void mma_role(uint32_t sbase, uint32_t tmem, const Wo
         for (int w = 0; w < kQTiles; ++w) {
             if (ok && j < wk.n[w]) {
                 if (j > 0) {
-                    ok = bounded_wait(b.s_free(w), (j - 1) & 1, abort_flag, kSiteSFree, true);
+                    ok = warp_wait(b.s_free(w), (j - 1) & 1, abort_flag, kSiteSFree);
                     if (!ok) break;
                     tc_fence_after();
                 }
@@ -327,16 +332,17 @@ __device__ __forceinline__ void mma_role(uint32_t sbase, uint32_t tmem, const Wo
                 const uint32_t tS = tmem + w * 256;
 #pragma unroll
                 for (int kk = 0; kk < D / 16; ++kk)  // K advance: 32 bytes inside the swizzled row
-                    umma_ss(tS, qdesc + 2 * kk, kdesc + 2 * kk, idesc_qk, kk > 0 ? 1u : 0u);
-                umma_commit(b.s_full(w));
+                    umma_ss_elect(tS, qdesc + 2 * kk, kdesc + 2 * kk, idesc_qk, kk > 0 ? 1u : 0u);
+                umma_commit_elect(b.s_full(w));
             }
         }
         if (ok && j > 0) ok = issue_pv<D>(j - 1, b, sbase, tmem, wk, abort_flag);
     }
     if (ok && wk.n_max > 0) issue_pv<D>(wk.n_max - 1, b, sbase, tmem, wk, abort_flag);
     // All issued MMAs must finish before TMEM and shared memory are released.
-    umma_commit(b.drain());
+    umma_commit_elect(b.drain());
     bounded_wait(b.drain(), 0, abort_flag, kSiteMmaDrain, false);
+    __syncwarp();
 }
 
 // ---------------------------------------------------------------------------
@@ -470,13 +476,16 @@ __device__ __forceinline__ void softmax_role(const FlashParams &p, uint32_t sbas
                 for (int c = 0; c < kBlockN; ++c) x[c] = c < lim ? x[c] : -INFINITY;
             }
         }
-        float mx0 = x[0], mx1 = x[1];
+        // row max: 8 independent 3-input max chains (short dependency chains)
+        float mx[8];
 #pragma unroll
-        for (int c = 2; c < kBlockN; c += 4) {
-            mx0 = fmax3(mx0, x[c], x[c + 1]);
-            mx1 = fmax3(mx1, x[c + 2], x[c + 3]);
+        for (int i = 0; i < 8; ++i) mx[i] = x[i];
+#pragma unroll
+        for (int c = 8; c < kBlockN; c += 16) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) mx[i] = fmax3(mx[i], x[c + 2 * i], x[c + 2 * i + 1]);
         }
-        const float m_tile = fmaxf(mx0, mx1) * kmul;
+        const float m_tile = fmaxf(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], fmax3(mx[5], mx[6], mx[7]))) * kmul;
         const float m_new = fmaxf(m, m_tile);
         const bool need = m_new > m + kRescaleThreshold;
         float m_use = need ? m_new : m;
@@ -484,17 +493,34 @@ __device__ __forceinline__ void softmax_role(const FlashParams &p, uint32_t sbas
         const float alpha = ex2_approx(m - m_use);  // 1 when not rescaling, 0 on the first tile
         const float neg_m = -m_use;
 
+        // Exp phase.  The two softmax warpgroups take turns (tile j of WG0, then tile j
+        // of WG1, then tile j+1 of WG0, ...) so the MUFU pipe serves one warpgroup at a
+        // time while the other loads S, reduces the max and stores P.
+        const int n_other = wk.n[w ^ 1];
+        if (w == 0 ? (j >= 1 && j - 1 < n_other) : (j < n_other)) {
+            ok = warp_wait(b.turn(w), (w == 0 ? j - 1 : j) & 1, abort_flag, kSiteTurn);
+            if (!ok) break;
+        }
         uint32_t pk[kBlockN / 2];
-        float sum0 = 0.0f, sum1 = 0.0f;
+        uint64_t sum2 = 0ull;  // (0.0f, 0.0f)
+        const uint64_t kmul2 = pack_f32x2(kmul, kmul), negm2 = pack_f32x2(neg_m, neg_m);
 #pragma unroll
         for (int c = 0; c < kBlockN / 2; ++c) {
-            const float p0 = ex2_approx(fmaf(x[2 * c], kmul, neg_m));
-            const float p1 = ex2_approx(fmaf(x[2 * c + 1], kmul, neg_m));
-            sum0 += p0;
-            sum1 += p1;
+            float e0, e1;
+            unpack_f32x2(ffma2(pack_f32x2(x[2 * c], x[2 * c + 1]), kmul2, negm2), e0, e1);
+            const float p0 = ex2_approx(e0);
+            const float p1 = ex2_approx(e1);
+            const uint64_t pp = pack_f32x2(p0, p1);
+            sum2 = fadd2(sum2, pp);
             pk[c] = pack_f16x2(p0, p1);  // P rounded to f16 (as src/flash_h64_bn32.zig:185)
         }
-        l = l * alpha + (sum0 + sum1);
+        __syncwarp();
+        if (w == 0 ? (j < n_other) : (j + 1 < n_other)) {
+            if (lane == 0) mbar_arrive(b.turn(w ^ 1));
+        }
+        float s0, s1;
+        unpack_f32x2(sum2, s0, s1);
+        l = l * alpha + (s0 + s1);
 
         if (j > 0) {
             // PV of the previous tile must be done: it reads P and accumulates into O.
@@ -559,6 +585,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(b.o_done(w), 1);
         }
         mbar_init(b.drain(), 1);
+        mbar_init(b.turn(0), 4);
+        mbar_init(b.turn(1), 4);
         *abort_flag = 0u;
         mbar_fence_init();
     }
@@ -578,14 +606,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == 0) {
         if constexpr (kTma) {
-            if (lane == 0) producer_tma<D>(&tmap_q, &tmap_k, &tmap_v, sbase, wk, abort_flag);
+            producer_tma<D>(&tmap_q, &tmap_k, &tmap_v, sbase, wk, abort_flag);
         } else {
             producer_lsu<D>(p, smem, sbase, wk, abort_flag, lane);
         }
         __syncwarp();
     } else if (warp == 1) {
-        if (lane == 0) mma_role<D>(sbase, tmem, wk, abort_flag);
-        __syncwarp();
+        mma_role<D>(sbase, tmem, wk, abort_flag);
     } else if (warp >= 4) {
         softmax_role<D>(p, sbase, tmem, wk, abort_flag, warp, lane);
     }
