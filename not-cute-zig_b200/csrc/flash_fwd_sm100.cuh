@@ -93,7 +93,7 @@ struct SmemLayout {
     static constexpr int kOffV = kOffK + kStages * kTile;
     static constexpr int kOffBar = kOffV + kStages * kTile;
     // barriers: q_full | k_full[S] | v_full[S] | kv_empty[S] | s_full[2] | s_free[2] | p_full[2] | o_done[2] | drain
-    //           | turn[2]
+    //           | turn[4][2]
     static constexpr int kBarQFull = 0;
     static constexpr int kBarKFull = 1;
     static constexpr int kBarVFull = kBarKFull + kStages;
@@ -103,8 +103,10 @@ struct SmemLayout {
     static constexpr int kBarPFull = kBarSFree + 2;
     static constexpr int kBarODone = kBarPFull + 2;
     static constexpr int kBarDrain = kBarODone + 2;
-    static constexpr int kBarTurn = kBarDrain + 1;  // exp-phase hand-off between the softmax warpgroups
-    static constexpr int kNumBars = kBarTurn + 2;
+    // exp-phase hand-off between softmax warps 4+i and 8+i, which share SM sub-partition i
+    // (and its MUFU unit): turn[i][w] completes when it is warp (4+4w+i)'s turn.
+    static constexpr int kBarTurn = kBarDrain + 1;
+    static constexpr int kNumBars = kBarTurn + 8;
     static constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
     static constexpr int kOffAbort = kOffTmemSlot + 4;
     static constexpr int kBytes = kOffAbort + 4;
@@ -142,9 +144,10 @@ __device__ __forceinline__ Work make_work(const FlashParams &p) {
 // Bounded mbarrier wait.  Returns false when the CTA is aborting or the wait
 // exceeded kWaitLimitNs (then it raises the abort flag and records the site).
 // honor_abort = false is used by teardown waits that must not be skipped.
-__device__ __noinline__ bool bounded_wait(uint32_t bar, uint32_t parity, volatile uint32_t *abort_flag,
-                                          uint32_t site, bool honor_abort) {
-    if (mbar_try_wait(bar, parity)) return true;
+// The slow loop is out of line; the common already-complete case costs one
+// inlined try_wait.
+__device__ __noinline__ bool bounded_wait_slow(uint32_t bar, uint32_t parity, volatile uint32_t *abort_flag,
+                                               uint32_t site, bool honor_abort) {
     const unsigned long long t0 = global_timer_ns();
     for (uint32_t it = 1;; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
@@ -157,6 +160,12 @@ __device__ __noinline__ bool bounded_wait(uint32_t bar, uint32_t parity, volatil
             }
         }
     }
+}
+
+__device__ __forceinline__ bool bounded_wait(uint32_t bar, uint32_t parity, volatile uint32_t *abort_flag,
+                                             uint32_t site, bool honor_abort) {
+    if (mbar_try_wait(bar, parity)) return true;
+    return bounded_wait_slow(bar, parity, abort_flag, site, honor_abort);
 }
 
 // All lanes wait; the result is made warp-uniform so .sync.aligned tcgen05
@@ -181,7 +190,7 @@ struct Bars {
     __device__ __forceinline__ uint32_t p_full(int w) const { return at(L::kBarPFull + w); }
     __device__ __forceinline__ uint32_t o_done(int w) const { return at(L::kBarODone + w); }
     __device__ __forceinline__ uint32_t drain() const { return at(L::kBarDrain); }
-    __device__ __forceinline__ uint32_t turn(int w) const { return at(L::kBarTurn + w); }
+    __device__ __forceinline__ uint32_t turn(int sub, int w) const { return at(L::kBarTurn + 2 * sub + w); }
 };
 
 // ---------------------------------------------------------------------------
@@ -477,13 +486,19 @@ __device__ __forceinline__ void softmax_role(const FlashParams &p, uint32_t sbas
             }
         }
         // row max: 8 independent 3-input max chains (short dependency chains)
+        // chain i covers x[i], x[8+i], ..., x[120+i]
+        static_assert(kBlockN % 16 == 8 || kBlockN % 16 == 0, "tile width");
         float mx[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) mx[i] = x[i];
 #pragma unroll
-        for (int c = 8; c < kBlockN; c += 16) {
+        for (int c = 8; c + 16 <= kBlockN; c += 16) {
 #pragma unroll
-            for (int i = 0; i < 8; ++i) mx[i] = fmax3(mx[i], x[c + 2 * i], x[c + 2 * i + 1]);
+            for (int i = 0; i < 8; ++i) mx[i] = fmax3(mx[i], x[c + i], x[c + 8 + i]);
+        }
+        if constexpr (kBlockN % 16 == 0) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) mx[i] = fmaxf(mx[i], x[kBlockN - 8 + i]);
         }
         const float m_tile = fmaxf(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], fmax3(mx[5], mx[6], mx[7]))) * kmul;
         const float m_new = fmaxf(m, m_tile);
@@ -493,12 +508,14 @@ __device__ __forceinline__ void softmax_role(const FlashParams &p, uint32_t sbas
         const float alpha = ex2_approx(m - m_use);  // 1 when not rescaling, 0 on the first tile
         const float neg_m = -m_use;
 
-        // Exp phase.  The two softmax warpgroups take turns (tile j of WG0, then tile j
-        // of WG1, then tile j+1 of WG0, ...) so the MUFU pipe serves one warpgroup at a
-        // time while the other loads S, reduces the max and stores P.
+        // Exp phase.  Warps 4+i (tile 0) and 8+i (tile 1) share SM sub-partition i and
+        // its MUFU unit; they take turns (tile j of warp 4+i, tile j of warp 8+i, tile
+        // j+1 of warp 4+i, ...) so one runs its exponentials while the other loads S,
+        // reduces the max and stores P.
         const int n_other = wk.n[w ^ 1];
+        const int sub = warp & 3;
         if (w == 0 ? (j >= 1 && j - 1 < n_other) : (j < n_other)) {
-            ok = warp_wait(b.turn(w), (w == 0 ? j - 1 : j) & 1, abort_flag, kSiteTurn);
+            ok = warp_wait(b.turn(sub, w), (w == 0 ? j - 1 : j) & 1, abort_flag, kSiteTurn);
             if (!ok) break;
         }
         uint32_t pk[kBlockN / 2];
@@ -516,7 +533,7 @@ __device__ __forceinline__ void softmax_role(const FlashParams &p, uint32_t sbas
         }
         __syncwarp();
         if (w == 0 ? (j < n_other) : (j + 1 < n_other)) {
-            if (lane == 0) mbar_arrive(b.turn(w ^ 1));
+            if (lane == 0) mbar_arrive(b.turn(sub, w ^ 1));
         }
         float s0, s1;
         unpack_f32x2(sum2, s0, s1);
@@ -585,8 +602,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(b.o_done(w), 1);
         }
         mbar_init(b.drain(), 1);
-        mbar_init(b.turn(0), 4);
-        mbar_init(b.turn(1), 4);
+        for (int i = 0; i < 8; ++i) mbar_init(b.at(L::kBarTurn + i), 1);
         *abort_flag = 0u;
         mbar_fence_init();
     }
