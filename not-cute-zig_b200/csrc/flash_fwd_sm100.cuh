@@ -50,6 +50,22 @@ constexpr int kThreads = 384;   // 12 warps
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleThreshold = 8.0f;        // log2 units
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait
+// Exponentials: in every group of kExp2EmuPeriod column pairs, the last
+// kExp2EmuCount pairs are computed by a polynomial on the FMA pipe instead of
+// the MUFU unit, which is the bottleneck of the softmax at head_dim <= 64.
+#ifndef NCZ_EXP2_EMU_PERIOD
+#define NCZ_EXP2_EMU_PERIOD 8
+#endif
+#ifndef NCZ_EXP2_EMU_COUNT
+#define NCZ_EXP2_EMU_COUNT 0
+#endif
+constexpr int kExp2EmuPeriod = NCZ_EXP2_EMU_PERIOD;
+constexpr int kExp2EmuCount = NCZ_EXP2_EMU_COUNT;
+// 1: the two softmax warps of an SM sub-partition take turns on the MUFU unit.
+#ifndef NCZ_EXP_TURNS
+#define NCZ_EXP_TURNS 0
+#endif
+constexpr bool kExpTurns = NCZ_EXP_TURNS != 0;
 
 // where a bounded wait gave up (bits 24..30 of the status word)
 enum WaitSite : uint32_t {
@@ -514,7 +530,7 @@ __device__ __forceinline__ void softmax_role(const FlashParams &p, uint32_t sbas
         // reduces the max and stores P.
         const int n_other = wk.n[w ^ 1];
         const int sub = warp & 3;
-        if (w == 0 ? (j >= 1 && j - 1 < n_other) : (j < n_other)) {
+        if (kExpTurns && (w == 0 ? (j >= 1 && j - 1 < n_other) : (j < n_other))) {
             ok = warp_wait(b.turn(sub, w), (w == 0 ? j - 1 : j) & 1, abort_flag, kSiteTurn);
             if (!ok) break;
         }
@@ -523,16 +539,20 @@ __device__ __forceinline__ void softmax_role(const FlashParams &p, uint32_t sbas
         const uint64_t kmul2 = pack_f32x2(kmul, kmul), negm2 = pack_f32x2(neg_m, neg_m);
 #pragma unroll
         for (int c = 0; c < kBlockN / 2; ++c) {
-            float e0, e1;
+            float e0, e1, p0, p1;
             unpack_f32x2(ffma2(pack_f32x2(x[2 * c], x[2 * c + 1]), kmul2, negm2), e0, e1);
-            const float p0 = ex2_approx(e0);
-            const float p1 = ex2_approx(e1);
+            if (kExp2EmuPeriod > 0 && c % kExp2EmuPeriod >= kExp2EmuPeriod - kExp2EmuCount) {
+                exp2_poly_x2(e0, e1, p0, p1);  // FMA pipe
+            } else {
+                p0 = ex2_approx(e0);  // MUFU
+                p1 = ex2_approx(e1);
+            }
             const uint64_t pp = pack_f32x2(p0, p1);
             sum2 = fadd2(sum2, pp);
             pk[c] = pack_f16x2(p0, p1);  // P rounded to f16 (as src/flash_h64_bn32.zig:185)
         }
         __syncwarp();
-        if (w == 0 ? (j < n_other) : (j + 1 < n_other)) {
+        if (kExpTurns && (w == 0 ? (j < n_other) : (j + 1 < n_other))) {
             if (lane == 0) mbar_arrive(b.turn(sub, w ^ 1));
         }
         float s0, s1;

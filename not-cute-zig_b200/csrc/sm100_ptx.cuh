@@ -85,6 +85,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// Non-blocking probe: true when the phase with `parity` has completed.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n"
+        ".reg .pred p;\n"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        "selp.u32 %0, 1, 0, p;\n"
+        "}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 // --------------------------------------------------------------------------
 // TMA (no multicast anywhere in this library)
 // --------------------------------------------------------------------------
@@ -308,6 +323,33 @@ __device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
     uint64_t d;
     asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
     return d;
+}
+// 2^e0, 2^e1 on the FMA pipe (no MUFU), for e <= 8:
+//   e = n + f with n = rint(e) (the 1.5 * 2^23 rounding trick) and f in [-1/2, 1/2];
+//   2^f ~ 1 + c1 f + c2 f^2 + c3 f^3 + c4 f^4, coefficients fitted here by a Remez
+//   exchange for minimax relative error on [-1/2, 1/2] with the constant term held
+//   at 1 (so 2^0 == 1 exactly); max relative error 3.7e-6 in f32;
+//   2^n is added to the exponent field as an integer (n << 23).
+// e is clamped to >= -125 so the exponent never underflows; -inf gives 2^-125.
+__device__ __forceinline__ void exp2_poly_x2(float e0, float e1, float &p0, float &p1) {
+    constexpr float kC1 = 0.6931135654449463f, kC2 = 0.2402070313692093f;
+    constexpr float kC3 = 0.05597792938351631f, kC4 = 0.009784870781004429f;
+    constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+    e0 = fmaxf(e0, -125.0f);
+    e1 = fmaxf(e1, -125.0f);
+    const uint64_t e = pack_f32x2(e0, e1);
+    const uint64_t t = fadd2(e, pack_f32x2(kRound, kRound));          // low mantissa bits hold n
+    const uint64_t n = fadd2(t, pack_f32x2(-kRound, -kRound));        // n as float
+    const uint64_t f = ffma2(n, pack_f32x2(-1.0f, -1.0f), e);         // e - n, exact
+    uint64_t q = ffma2(f, pack_f32x2(kC4, kC4), pack_f32x2(kC3, kC3));
+    q = ffma2(q, f, pack_f32x2(kC2, kC2));
+    q = ffma2(q, f, pack_f32x2(kC1, kC1));
+    q = ffma2(q, f, pack_f32x2(1.0f, 1.0f));
+    float q0, q1, t0, t1;
+    unpack_f32x2(q, q0, q1);
+    unpack_f32x2(t, t0, t1);
+    p0 = __int_as_float(__float_as_int(q0) + (__float_as_int(t0) << 23));
+    p1 = __int_as_float(__float_as_int(q1) + (__float_as_int(t1) << 23));
 }
 // Packs two floats into f16x2 (round to nearest even): `lo` in bits 0..15.
 __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
