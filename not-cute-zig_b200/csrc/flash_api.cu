@@ -28,6 +28,7 @@ using ncz::FlashParams;
 using ncz::SmemLayout;
 
 constexpr int kMaxDevices = 64;
+constexpr size_t kGroupRows = static_cast<size_t>(ncz::kBlockM) * ncz::kQTiles;  // Q rows per CTA
 constexpr int kVariants = 6;  // (D in 16/32/64) x (TMA, LSU)
 
 std::mutex g_mu;
@@ -96,9 +97,9 @@ int validate_resolved(const Resolved &r) {
     if (r.producer < NCZ_PRODUCER_AUTO || r.producer > NCZ_PRODUCER_LSU) return NCZ_ERROR_INVALID_VALUE;
     // Implementation limits of the 32-bit tile / grid indices.
     if (r.seq > (size_t(1) << 30)) return NCZ_ERROR_INVALID_VALUE;
-    const size_t pairs = (r.seq + 255) / 256;
+    const size_t groups = (r.seq + kGroupRows - 1) / kGroupRows;
     size_t grid;
-    if (!mul_ok(pairs, r.bh, &grid) || grid > size_t(0x7FFFFFFF)) return NCZ_ERROR_INVALID_VALUE;
+    if (!mul_ok(groups, r.bh, &grid) || grid > size_t(0x7FFFFFFF)) return NCZ_ERROR_INVALID_VALUE;
     if (r.bh > size_t(0x7FFFFFFF)) return NCZ_ERROR_INVALID_VALUE;
     return NCZ_SUCCESS;
 }
@@ -120,11 +121,12 @@ Resolved from_desc(const ncz_flash_desc &d) {
 
 bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
-// 3-D map over one operand: dims (d, seq, bh), box (d, 128, 1), swizzle = row width.
-bool encode_map(CUtensorMap *map, const void *ptr, size_t d, size_t seq, size_t bh, size_t row, size_t slice) {
+// 3-D map over one operand: dims (d, seq, bh), box (d, box_rows, 1), swizzle = row width.
+bool encode_map(CUtensorMap *map, const void *ptr, size_t d, size_t seq, size_t bh, size_t row, size_t slice,
+                uint32_t box_rows) {
     cuuint64_t dims[3] = {d, seq, bh};
     cuuint64_t strides[2] = {row * 2, slice * 2};
-    cuuint32_t box[3] = {static_cast<cuuint32_t>(d), 128u, 1u};
+    cuuint32_t box[3] = {static_cast<cuuint32_t>(d), box_rows, 1u};
     cuuint32_t estr[3] = {1u, 1u, 1u};
     const CUtensorMapSwizzle swz = d == 64 ? CU_TENSOR_MAP_SWIZZLE_128B
                                            : (d == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
@@ -169,9 +171,9 @@ int launch_on_current(const Resolved &r, int dev) {
     std::memset(&tk, 0, sizeof(tk));
     std::memset(&tv, 0, sizeof(tv));
     if (use_tma) {
-        const bool enc = encode_map(&tq, r.q, r.d, r.seq, r.bh, r.qr, r.qs) &&
-                         encode_map(&tk, r.k, r.d, r.seq, r.bh, r.kr, r.ks) &&
-                         encode_map(&tv, r.v, r.d, r.seq, r.bh, r.vr, r.vs);
+        const bool enc = encode_map(&tq, r.q, r.d, r.seq, r.bh, r.qr, r.qs, ncz::kBlockM) &&
+                         encode_map(&tk, r.k, r.d, r.seq, r.bh, r.kr, r.ks, ncz::kBlockN) &&
+                         encode_map(&tv, r.v, r.d, r.seq, r.bh, r.vr, r.vs, ncz::kBlockN);
         if (!enc) {
             if (r.producer == NCZ_PRODUCER_TMA) return NCZ_ERROR_MISALIGNED;
             use_tma = false;  // e.g. strides the TMA unit cannot express: plain-load producer
@@ -193,13 +195,13 @@ int launch_on_current(const Resolved &r, int dev) {
     p.o_row = static_cast<long long>(r.orow);
     p.seq_len = static_cast<int>(r.seq);
     p.batch_heads = static_cast<int>(r.bh);
-    p.num_pairs = static_cast<int>((r.seq + 255) / 256);
+    p.num_groups = static_cast<int>((r.seq + kGroupRows - 1) / kGroupRows);
     p.scale_log2 = static_cast<float>(static_cast<double>(r.scale) * 1.4426950408889634);
     p.causal = r.causal != 0;
     p.o_f16 = r.o_dtype == NCZ_DTYPE_F16;
     const size_t vec_elems = p.o_f16 ? 8 : 4;
     p.o_vec = aligned(r.o, 16) && r.os % vec_elems == 0 && r.orow % vec_elems == 0;
-    const unsigned grid = static_cast<unsigned>(static_cast<size_t>(p.num_pairs) * r.bh);
+    const unsigned grid = static_cast<unsigned>(static_cast<size_t>(p.num_groups) * r.bh);
 
     switch (r.d) {
         case 16: return use_tma ? launch_variant<16, true>(tq, tk, tv, p, grid, dev, r.stream)

@@ -7,31 +7,31 @@
 // reach shared memory (TMA, or plain loads for misaligned strides).
 //
 // Work unit: one CTA per (batch x head slice, pair of 128-row Q tiles).  Q
-// tile w (w = 0, 1) covers rows q_base + 128 w .. + 127.  K/V stream through
-// a STAGES-deep ring of 128-key tiles shared by both Q tiles.
+// tile w covers rows q_base + 128 w .. + 127.  K/V stream through a
+// kStages-deep ring of 128-key tiles shared by both Q tiles of the CTA.
 //
 // Warp roles (384 threads):
-//   warp 0      producer: TMA or LSU loads of Q, K, V
-//   warp 1      TMEM allocator + tcgen05 MMA issuer
-//   (both run as whole warps; elect.sync picks the lane that issues)
-//   warps 2,3   idle (keep the softmax warpgroups warpgroup-aligned)
-//   warps 4-7   softmax for Q tile 0 (thread = row = TMEM lane)
-//   warps 8-11  softmax for Q tile 1
+//   warp 0       producer: TMA or LSU loads of Q, K, V
+//   warp 1       TMEM allocator + tcgen05 MMA issuer for Q tile 0
+//   warp 2       tcgen05 MMA issuer for Q tile 1
+//   (all run as whole warps; elect.sync picks the lane that issues)
+//   warp 3       idle (keeps the softmax warpgroups warpgroup-aligned)
+//   warpgroup 1+w softmax for Q tile w (thread = row = TMEM lane)
 //
-// TMEM (512 columns): per Q tile w, at column 256 w:
-//   S [0,128)   f32 scores of the current K tile     (QK^T, M=128 N=128)
-//   P [128,192) f16x2 probabilities, A operand of PV (aliasing nothing)
-//   O [192,192+D) f32 output accumulator             (PV, M=128 N=D)
+// TMEM (512 columns): per Q tile w the scores S_w (128 cols f32, QK^T, M=128
+// N=128), the probabilities P_w (128 f16 keys = 64 cols, the A operand of PV
+// read from TMEM) and O_w (D <= 64 cols f32, PV, M=128 N=D).  The softmax
+// releases S_w as soon as the scores are in registers, so the MMA warp of Q
+// tile w issues QK_w(j+1) while the softmax is still exponentiating tile j;
+// PV_w(j) follows once P_w(j) is stored.  Each Q tile has its own MMA warp,
+// so neither tile's hand-offs wait behind the other's.
 //
-// Per K tile j the MMA warp issues S_w = Q_w K_j^T for both tiles, then
-// O_w += P_w(j-1) V_(j-1), so the tensor core computes tile j's scores while
-// the softmax warps work on tile j-1.  Online softmax (reference:
-// src/flash_h64_bn32.zig:139-211) keeps the row max m (log2 domain) and
-// row sum l in registers.  O is rescaled in TMEM only when the row max
-// grows by more than 2^8 since the last rescale (the exponent base is stale
-// by at most 8, so P <= 256 fits f16 and the final O / l is unchanged).
+// Online softmax (reference: src/flash_h64_bn32.zig:139-211) keeps the
+// exponent base m (log2 domain) and the row sum l in registers; O is
+// rescaled in TMEM only when the row max grows by more than 2^8 since the
+// last rescale (P <= 2^8 then still fits f16, and O / l is unchanged).
 //
-// Every mbarrier wait is bounded (kWaitLimitNs).  On expiry the waiter
+// Every mbarrier wait is bounded (kWaitLimitCycles).  On expiry the waiter
 // records where it gave up in g_ncz_status, raises a CTA-wide abort flag and
 // all roles leave their loops; issued copies and MMAs are waited for
 // (bounded) before TMEM is freed and the CTA exits.  No trap, no assert.
@@ -43,16 +43,23 @@
 
 namespace ncz {
 
-constexpr int kBlockM = 128;    // rows per Q tile = TMEM lanes
-constexpr int kBlockN = 128;    // keys per K/V tile
-constexpr int kQTiles = 2;      // Q tiles per CTA
-constexpr int kThreads = 384;   // 12 warps
+constexpr int kBlockM = 128;  // rows per Q tile = TMEM lanes
+constexpr int kBlockN = 128;  // keys per K/V tile
+constexpr int kQTiles = 2;    // Q tiles per CTA
+constexpr int kThreads = 128 * (1 + kQTiles);
 constexpr uint32_t kTmemCols = 512;
-constexpr float kRescaleThreshold = 8.0f;        // log2 units
-constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait
+// TMEM column map per Q tile w (base kTileCols * w): S | P | O
+constexpr uint32_t kColP = kBlockN;               // f16 pairs: kBlockN / 2 columns
+constexpr uint32_t kColO = kColP + kBlockN / 2;
+constexpr uint32_t kTileCols = kColO + 64;
+static_assert(kQTiles * kTileCols <= kTmemCols, "TMEM budget");
+constexpr float kRescaleThreshold = 8.0f;                   // log2 units
+constexpr float kMaxP = 256.0f;                             // 2^kRescaleThreshold
+// Spin-wait bound in SM cycles (about 2 s at 2 GHz; longer at lower clocks).
+constexpr unsigned long long kWaitLimitCycles = 4000000000ull;
 // Exponentials: in every group of kExp2EmuPeriod column pairs, the last
 // kExp2EmuCount pairs are computed by a polynomial on the FMA pipe instead of
-// the MUFU unit, which is the bottleneck of the softmax at head_dim <= 64.
+// the MUFU unit.  Off by default: measured slower than MUFU-only here.
 #ifndef NCZ_EXP2_EMU_PERIOD
 #define NCZ_EXP2_EMU_PERIOD 8
 #endif
@@ -61,7 +68,7 @@ constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s per wait
 #endif
 constexpr int kExp2EmuPeriod = NCZ_EXP2_EMU_PERIOD;
 constexpr int kExp2EmuCount = NCZ_EXP2_EMU_COUNT;
-// 1: the two softmax warps of an SM sub-partition take turns on the MUFU unit.
+// 1: the two softmax warps of an SM sub-partition take turns on its MUFU unit.
 #ifndef NCZ_EXP_TURNS
 #define NCZ_EXP_TURNS 0
 #endif
@@ -91,42 +98,46 @@ struct FlashParams {
     long long q_row, k_row, v_row, o_row;              // per row, elements
     int seq_len;
     int batch_heads;
-    int num_pairs;   // ceil(seq_len / 256)
+    int num_groups;    // ceil(seq_len / 256)
     float scale_log2;  // scale * log2(e)
     int causal;
     int o_f16;
-    int o_vec;   // 16-byte vector stores of O are aligned
+    int o_vec;  // 16-byte vector stores of O are aligned
 };
 
 template <int D>
 struct SmemLayout {
-    static constexpr int kSpan = 2 * D;                  // bytes per row = swizzle width
-    static constexpr int kTile = kBlockN * kSpan;        // one 128-row tile
-    static constexpr int kStages = D == 64 ? 3 : (D == 32 ? 4 : 6);
+    static constexpr int kSpan = 2 * D;              // bytes per row = swizzle width
+    static constexpr int kQTile = kBlockM * kSpan;   // one 128-row Q tile
+    static constexpr int kKvTile = kBlockN * kSpan;  // one K or V tile
+    // K/V ring: 128 KB at d=64, 64 KB below, at most 8 stages
+    static constexpr int kStagesRaw = (D == 64 ? 128 * 1024 : 64 * 1024) / (2 * kKvTile);
+    static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
     static constexpr uint32_t kUmmaLayout = D == 64 ? 2u : (D == 32 ? 4u : 6u);
     static constexpr int kOffQ = 0;
-    static constexpr int kOffK = kOffQ + kQTiles * kTile;
-    static constexpr int kOffV = kOffK + kStages * kTile;
-    static constexpr int kOffBar = kOffV + kStages * kTile;
-    // barriers: q_full | k_full[S] | v_full[S] | kv_empty[S] | s_full[2] | s_free[2] | p_full[2] | o_done[2] | drain
-    //           | turn[4][2]
+    static constexpr int kOffK = kOffQ + kQTiles * kQTile;
+    static constexpr int kOffV = kOffK + kStages * kKvTile;
+    static constexpr int kOffBar = kOffV + kStages * kKvTile;
+    // barriers: q_full | k_full[S] | v_full[S] | kv_empty[S] | s_full[Q] | s_free[Q] | p_full[Q] | o_done[Q]
+    //           | drain[Q] | turn[4][Q]
     static constexpr int kBarQFull = 0;
     static constexpr int kBarKFull = 1;
     static constexpr int kBarVFull = kBarKFull + kStages;
     static constexpr int kBarKvEmpty = kBarVFull + kStages;
     static constexpr int kBarSFull = kBarKvEmpty + kStages;
-    static constexpr int kBarSFree = kBarSFull + 2;
-    static constexpr int kBarPFull = kBarSFree + 2;
-    static constexpr int kBarODone = kBarPFull + 2;
-    static constexpr int kBarDrain = kBarODone + 2;
-    // exp-phase hand-off between softmax warps 4+i and 8+i, which share SM sub-partition i
-    // (and its MUFU unit): turn[i][w] completes when it is warp (4+4w+i)'s turn.
-    static constexpr int kBarTurn = kBarDrain + 1;
-    static constexpr int kNumBars = kBarTurn + 8;
+    static constexpr int kBarSFree = kBarSFull + kQTiles;
+    static constexpr int kBarPFull = kBarSFree + kQTiles;
+    static constexpr int kBarODone = kBarPFull + kQTiles;
+    static constexpr int kBarDrain = kBarODone + kQTiles;  // one per MMA warp
+    // turn[i][w]: Q tile w's softmax warp on sub-partition i may use the MUFU unit
+    static constexpr int kBarTurn = kBarDrain + kQTiles;
+    static constexpr int kNumBars = kBarTurn + 4 * kQTiles;
     static constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
     static constexpr int kOffAbort = kOffTmemSlot + 4;
     static constexpr int kBytes = kOffAbort + 4;
     static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
+    static_assert(kStages >= 2, "K/V ring");
+    static_assert(kAlloc <= 227 * 1024, "shared memory");
 };
 
 struct Work {
@@ -141,35 +152,36 @@ __device__ uint32_t g_ncz_status = 0u;
 __device__ __forceinline__ Work make_work(const FlashParams &p) {
     Work wk;
     const int item = static_cast<int>(blockIdx.x);
-    // Heaviest (last) Q-tile pairs first: under causal masking they visit the most K tiles.
-    const int pair = p.num_pairs - 1 - item / p.batch_heads;
+    // Heaviest (last) Q-tile groups first: under causal masking they visit the most K tiles.
+    const int group = p.num_groups - 1 - item / p.batch_heads;
     wk.slice = item % p.batch_heads;
-    wk.q_base = pair * (kQTiles * kBlockM);
+    wk.q_base = group * (kQTiles * kBlockM);
     const int n_kv = (p.seq_len + kBlockN - 1) / kBlockN;
     wk.n_max = 0;
 #pragma unroll
     for (int w = 0; w < kQTiles; ++w) {
         const int q0 = wk.q_base + w * kBlockM;
+        const int last_row = min(q0 + kBlockM, p.seq_len) - 1;
         // causal (reference tile_end, src/flash_h64_bn32.zig:80-84): K tiles up to the diagonal
-        wk.n[w] = q0 >= p.seq_len ? 0 : (p.causal ? q0 / kBlockN + 1 : n_kv);
+        wk.n[w] = q0 >= p.seq_len ? 0 : (p.causal ? last_row / kBlockN + 1 : n_kv);
         wk.n_max = wk.n[w] > wk.n_max ? wk.n[w] : wk.n_max;
     }
     return wk;
 }
 
 // Bounded mbarrier wait.  Returns false when the CTA is aborting or the wait
-// exceeded kWaitLimitNs (then it raises the abort flag and records the site).
+// exceeded kWaitLimitCycles (then it raises the abort flag and records the site).
 // honor_abort = false is used by teardown waits that must not be skipped.
 // The slow loop is out of line; the common already-complete case costs one
 // inlined try_wait.
 __device__ __noinline__ bool bounded_wait_slow(uint32_t bar, uint32_t parity, volatile uint32_t *abort_flag,
                                                uint32_t site, bool honor_abort) {
-    const unsigned long long t0 = global_timer_ns();
+    const unsigned long long t0 = sm_clock();
     for (uint32_t it = 1;; ++it) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((it & 15u) == 0u) {
             if (honor_abort && *abort_flag) return false;
-            if (global_timer_ns() - t0 > kWaitLimitNs) {
+            if (sm_clock() - t0 > kWaitLimitCycles) {
                 *abort_flag = 1u;
                 atomicCAS(&g_ncz_status, 0u, 0x80000000u | (site << 24) | (blockIdx.x & 0xFFFFFFu));
                 return false;
@@ -205,36 +217,35 @@ struct Bars {
     __device__ __forceinline__ uint32_t s_free(int w) const { return at(L::kBarSFree + w); }
     __device__ __forceinline__ uint32_t p_full(int w) const { return at(L::kBarPFull + w); }
     __device__ __forceinline__ uint32_t o_done(int w) const { return at(L::kBarODone + w); }
-    __device__ __forceinline__ uint32_t drain() const { return at(L::kBarDrain); }
-    __device__ __forceinline__ uint32_t turn(int sub, int w) const { return at(L::kBarTurn + 2 * sub + w); }
+    __device__ __forceinline__ uint32_t drain(int w) const { return at(L::kBarDrain + w); }
+    __device__ __forceinline__ uint32_t turn(int sub, int w) const { return at(L::kBarTurn + kQTiles * sub + w); }
 };
 
 // ---------------------------------------------------------------------------
 // producer, TMA variant (whole warp; elect.sync picks the issuing lane)
 // ---------------------------------------------------------------------------
 template <int D>
-__device__ __forceinline__ void producer_tma(const CUtensorMap *tq, const CUtensorMap *tk,
-                                             const CUtensorMap *tv, uint32_t sbase, const Work &wk,
-                                             volatile uint32_t *abort_flag) {
+__device__ __forceinline__ void producer_tma(const CUtensorMap *tq, const CUtensorMap *tk, const CUtensorMap *tv,
+                                             uint32_t sbase, const Work &wk, volatile uint32_t *abort_flag) {
     using L = SmemLayout<D>;
     const Bars<D> b{sbase};
     uint32_t qbytes = 0;
 #pragma unroll
-    for (int w = 0; w < kQTiles; ++w) qbytes += wk.n[w] > 0 ? L::kTile : 0;
+    for (int w = 0; w < kQTiles; ++w) qbytes += wk.n[w] > 0 ? L::kQTile : 0;
     mbar_arrive_expect_tx_elect(b.q_full(), qbytes);
 #pragma unroll
     for (int w = 0; w < kQTiles; ++w)
         if (wk.n[w] > 0)
-            tma_load_3d_elect(sbase + L::kOffQ + w * L::kTile, tq, b.q_full(), 0, wk.q_base + w * kBlockM, wk.slice);
+            tma_load_3d_elect(sbase + L::kOffQ + w * L::kQTile, tq, b.q_full(), 0, wk.q_base + w * kBlockM, wk.slice);
     int j = 0;
     for (; j < wk.n_max; ++j) {
         const int st = j % L::kStages;
         if (j >= L::kStages && !warp_wait(b.kv_empty(st), ((j / L::kStages) - 1) & 1, abort_flag, kSiteKvEmpty))
             break;
-        mbar_arrive_expect_tx_elect(b.k_full(st), L::kTile);
-        tma_load_3d_elect(sbase + L::kOffK + st * L::kTile, tk, b.k_full(st), 0, j * kBlockN, wk.slice);
-        mbar_arrive_expect_tx_elect(b.v_full(st), L::kTile);
-        tma_load_3d_elect(sbase + L::kOffV + st * L::kTile, tv, b.v_full(st), 0, j * kBlockN, wk.slice);
+        mbar_arrive_expect_tx_elect(b.k_full(st), L::kKvTile);
+        tma_load_3d_elect(sbase + L::kOffK + st * L::kKvTile, tk, b.k_full(st), 0, j * kBlockN, wk.slice);
+        mbar_arrive_expect_tx_elect(b.v_full(st), L::kKvTile);
+        tma_load_3d_elect(sbase + L::kOffV + st * L::kKvTile, tv, b.v_full(st), 0, j * kBlockN, wk.slice);
     }
     // Every issued copy must land before shared memory is released.
     bounded_wait(b.q_full(), 0, abort_flag, kSiteProducerDrain, false);
@@ -250,14 +261,14 @@ __device__ __forceinline__ void producer_tma(const CUtensorMap *tq, const CUtens
 // ---------------------------------------------------------------------------
 // producer, LSU variant (all 32 lanes): any 2-byte-aligned layout
 // ---------------------------------------------------------------------------
-// Loads rows row0 .. row0+127 of one slice (rows >= seq_len read as zero)
+// Loads rows row0 .. row0+kRows-1 of one slice (rows >= seq_len read as zero)
 // into a 1024-byte-aligned tile, in the same swizzled layout TMA produces.
-template <int D>
+template <int D, int kRows>
 __device__ __forceinline__ void lsu_tile(uint8_t *dst, const uint16_t *src, long long row_stride, int row0,
                                          int seq_len, int lane) {
     constexpr int kChunks = D / 8;  // 16-byte chunks per row
     constexpr uint32_t kSpan = 2 * D;
-    for (int idx = lane; idx < kBlockN * kChunks; idx += 32) {
+    for (int idx = lane; idx < kRows * kChunks; idx += 32) {
         const int r = idx / kChunks, c = idx % kChunks;
         const int grow = row0 + r;
         uint32_t wv[4] = {0u, 0u, 0u, 0u};
@@ -282,7 +293,9 @@ __device__ __forceinline__ void producer_lsu(const FlashParams &p, uint8_t *smem
     const uint16_t *vs = p.v + wk.slice * p.v_stride;
 #pragma unroll
     for (int w = 0; w < kQTiles; ++w)
-        if (wk.n[w] > 0) lsu_tile<D>(smem + L::kOffQ + w * L::kTile, qs, p.q_row, wk.q_base + w * kBlockM, p.seq_len, lane);
+        if (wk.n[w] > 0)
+            lsu_tile<D, kBlockM>(smem + L::kOffQ + w * L::kQTile, qs, p.q_row, wk.q_base + w * kBlockM, p.seq_len,
+                                 lane);
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) mbar_arrive(b.q_full());
@@ -290,11 +303,11 @@ __device__ __forceinline__ void producer_lsu(const FlashParams &p, uint8_t *smem
         const int st = j % L::kStages;
         if (j >= L::kStages && !warp_wait(b.kv_empty(st), ((j / L::kStages) - 1) & 1, abort_flag, kSiteKvEmpty))
             break;
-        lsu_tile<D>(smem + L::kOffK + st * L::kTile, ks, p.k_row, j * kBlockN, p.seq_len, lane);
+        lsu_tile<D, kBlockN>(smem + L::kOffK + st * L::kKvTile, ks, p.k_row, j * kBlockN, p.seq_len, lane);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(b.k_full(st));
-        lsu_tile<D>(smem + L::kOffV + st * L::kTile, vs, p.v_row, j * kBlockN, p.seq_len, lane);
+        lsu_tile<D, kBlockN>(smem + L::kOffV + st * L::kKvTile, vs, p.v_row, j * kBlockN, p.seq_len, lane);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(b.v_full(st));
@@ -305,68 +318,80 @@ __device__ __forceinline__ void producer_lsu(const FlashParams &p, uint8_t *smem
 // MMA issuer (whole warp; elect.sync picks the issuing lane)
 // ---------------------------------------------------------------------------
 template <int D>
-__device__ __forceinline__ bool issue_pv(int t, const Bars<D> &b, uint32_t sbase, uint32_t tmem, const Work &wk,
-                                         volatile uint32_t *abort_flag) {
+__device__ __forceinline__ void issue_qk(int j, uint32_t sbase, uint32_t tS, uint64_t qdesc) {
     using L = SmemLayout<D>;
-    const int st = t % L::kStages;
-    if (!warp_wait(b.v_full(st), (t / L::kStages) & 1, abort_flag, kSiteVFull)) return false;
-    tc_fence_after();
-    constexpr uint32_t idesc_pv = umma_idesc_f16_f32(kBlockM, D, 0, 1);  // B = V, MN-major
-    // V tile: 128 keys x D, rows of 2D bytes (one swizzle atom wide); 8-row groups 8*span apart.
-    const uint64_t vdesc = umma_smem_desc(sbase + L::kOffV + st * L::kTile, L::kTile, 8 * L::kSpan, L::kUmmaLayout);
-#pragma unroll
-    for (int w = 0; w < kQTiles; ++w) {
-        if (t < wk.n[w]) {
-            if (!warp_wait(b.p_full(w), t & 1, abort_flag, kSitePFull)) return false;
-            tc_fence_after();
-            const uint32_t tP = tmem + w * 256 + 128, tO = tmem + w * 256 + 192;
-#pragma unroll
-            for (int kk = 0; kk < kBlockN / 16; ++kk)
-                umma_ts_elect(tO, tP + kk * 8, vdesc + static_cast<uint64_t>((kk * 16 * L::kSpan) >> 4), idesc_pv,
-                              (t > 0 || kk > 0) ? 1u : 0u);
-            umma_commit_elect(b.o_done(w));
-        }
-    }
-    umma_commit_elect(b.kv_empty(st));
-    return true;
+    constexpr uint32_t idesc_qk = umma_idesc_f16_f32(kBlockM, kBlockN, 0, 0);  // both K-major
+    const int st = j % L::kStages;
+    const uint64_t kdesc = umma_smem_desc(sbase + L::kOffK + st * L::kKvTile, 16, 8 * L::kSpan, L::kUmmaLayout);
+    // K advance: 32 bytes (2 encoded units) inside the swizzled row per step
+    umma_ss_chain_elect<D / 16>(tS, qdesc, kdesc, idesc_qk);
 }
 
 template <int D>
-__device__ __forceinline__ void mma_role(uint32_t sbase, uint32_t tmem, const Work &wk, volatile uint32_t *abort_flag) {
+__device__ __forceinline__ void issue_pv(int j, uint32_t sbase, uint32_t tP, uint32_t tO) {
+    using L = SmemLayout<D>;
+    constexpr uint32_t idesc_pv = umma_idesc_f16_f32(kBlockM, D, 0, 1);  // B = V, MN-major
+    const int st = j % L::kStages;
+    // V tile: kBlockN keys x D, rows of 2D bytes (one swizzle atom wide); 8-row groups 8*span apart.
+    const uint64_t vdesc =
+        umma_smem_desc(sbase + L::kOffV + st * L::kKvTile, L::kKvTile, 8 * L::kSpan, L::kUmmaLayout);
+    // 16 keys per step: 8 TMEM columns of P, 16 rows of V
+    umma_ts_chain_elect<kBlockN / 16>(tO, tP, vdesc, static_cast<uint64_t>((16 * L::kSpan) >> 4), idesc_pv,
+                                      j > 0 ? 1u : 0u);
+}
+
+// One MMA warp per Q tile w (warps 1 and 2).  Per K tile j: QK_w(j+1) as soon
+// as the softmax has read S_w(j) and K(j+1) is resident, then PV_w(j) once
+// P_w(j) is stored and V(j) is resident.  Each warp arrives once per K tile on
+// the stage's kv_empty barrier (a commit after its PV, or a plain arrive past
+// its causal range), so a stage is released when both Q tiles are done with it.
+template <int D>
+__device__ __forceinline__ void mma_role(int w, uint32_t sbase, uint32_t tmem, const Work &wk,
+                                         volatile uint32_t *abort_flag, int lane) {
     using L = SmemLayout<D>;
     const Bars<D> b{sbase};
-    constexpr uint32_t idesc_qk = umma_idesc_f16_f32(kBlockM, kBlockN, 0, 0);  // both K-major
-    bool ok = warp_wait(b.q_full(), 0, abort_flag, kSiteQFull);
-    if (ok) tc_fence_after();
-    for (int j = 0; ok && j < wk.n_max; ++j) {
+    const int n = wk.n[w];
+    const uint32_t tS = tmem + w * kTileCols, tP = tS + kColP, tO = tS + kColO;
+    const uint64_t qdesc = umma_smem_desc(sbase + L::kOffQ + w * L::kQTile, 16, 8 * L::kSpan, L::kUmmaLayout);
+    bool ok = true;
+    if (n > 0) {
+        ok = warp_wait(b.q_full(), 0, abort_flag, kSiteQFull) && warp_wait(b.k_full(0), 0, abort_flag, kSiteKFull);
+        if (ok) {
+            tc_fence_after();
+            issue_qk<D>(0, sbase, tS, qdesc);
+            umma_commit_elect(b.s_full(w));
+        }
+    }
+    int j = 0;
+    for (; ok && j < n; ++j) {
         const int st = j % L::kStages;
-        ok = warp_wait(b.k_full(st), (j / L::kStages) & 1, abort_flag, kSiteKFull);
+        if (j + 1 < n) {
+            const int st1 = (j + 1) % L::kStages;
+            ok = warp_wait(b.s_free(w), j & 1, abort_flag, kSiteSFree) &&
+                 warp_wait(b.k_full(st1), ((j + 1) / L::kStages) & 1, abort_flag, kSiteKFull);
+            if (!ok) break;
+            tc_fence_after();
+            issue_qk<D>(j + 1, sbase, tS, qdesc);
+            umma_commit_elect(b.s_full(w));
+        }
+        ok = warp_wait(b.v_full(st), (j / L::kStages) & 1, abort_flag, kSiteVFull) &&
+             warp_wait(b.p_full(w), j & 1, abort_flag, kSitePFull);
         if (!ok) break;
         tc_fence_after();
-        const uint64_t kdesc = umma_smem_desc(sbase + L::kOffK + st * L::kTile, 16, 8 * L::kSpan, L::kUmmaLayout);
-#pragma unroll
-        for (int w = 0; w < kQTiles; ++w) {
-            if (ok && j < wk.n[w]) {
-                if (j > 0) {
-                    ok = warp_wait(b.s_free(w), (j - 1) & 1, abort_flag, kSiteSFree);
-                    if (!ok) break;
-                    tc_fence_after();
-                }
-                const uint64_t qdesc =
-                    umma_smem_desc(sbase + L::kOffQ + w * L::kTile, 16, 8 * L::kSpan, L::kUmmaLayout);
-                const uint32_t tS = tmem + w * 256;
-#pragma unroll
-                for (int kk = 0; kk < D / 16; ++kk)  // K advance: 32 bytes inside the swizzled row
-                    umma_ss_elect(tS, qdesc + 2 * kk, kdesc + 2 * kk, idesc_qk, kk > 0 ? 1u : 0u);
-                umma_commit_elect(b.s_full(w));
-            }
-        }
-        if (ok && j > 0) ok = issue_pv<D>(j - 1, b, sbase, tmem, wk, abort_flag);
+        issue_pv<D>(j, sbase, tP, tO);
+        umma_commit_elect(b.o_done(w));
+        umma_commit_elect(b.kv_empty(st));  // this Q tile is done with K(j) and V(j)
     }
-    if (ok && wk.n_max > 0) issue_pv<D>(wk.n_max - 1, b, sbase, tmem, wk, abort_flag);
+    // K tiles beyond this Q tile's causal range: release them on its behalf, once
+    // each is loaded (so the arrival counts toward that tile's use of the stage).
+    for (; ok && j < wk.n_max; ++j) {
+        ok = warp_wait(b.k_full(j % L::kStages), (j / L::kStages) & 1, abort_flag, kSiteKFull);
+        if (ok && lane == 0) mbar_arrive(b.kv_empty(j % L::kStages));
+        __syncwarp();
+    }
     // All issued MMAs must finish before TMEM and shared memory are released.
-    umma_commit_elect(b.drain());
-    bounded_wait(b.drain(), 0, abort_flag, kSiteMmaDrain, false);
+    umma_commit_elect(b.drain(w));
+    bounded_wait(b.drain(w), 0, abort_flag, kSiteMmaDrain, false);
     __syncwarp();
 }
 
@@ -379,54 +404,46 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
     return d;
 }
 
-template <int D>
-__device__ __forceinline__ void load_o_row(uint32_t taddr, float (&o)[D]) {
-    if constexpr (D == 64) {
-        uint32_t r[64];
+// TMEM load / store of one row's O columns
+template <int N>
+__device__ __forceinline__ void load_cols(uint32_t taddr, float (&o)[N]) {
+    uint32_t r[N];
+    if constexpr (N == 64) {
         tmem_ld_x64_wait(taddr, r);
-#pragma unroll
-        for (int i = 0; i < 64; ++i) o[i] = __uint_as_float(r[i]);
-    } else if constexpr (D == 32) {
-        uint32_t r[32];
+    } else if constexpr (N == 32) {
         tmem_ld_x32_wait(taddr, r);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] = __uint_as_float(r[i]);
     } else {
-        uint32_t r[16];
+        static_assert(N == 16, "column count");
         tmem_ld_x16_wait(taddr, r);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) o[i] = __uint_as_float(r[i]);
     }
+#pragma unroll
+    for (int i = 0; i < N; ++i) o[i] = __uint_as_float(r[i]);
 }
 
-template <int D>
-__device__ __forceinline__ void store_o_row(uint32_t taddr, const float (&o)[D]) {
-    if constexpr (D == 64) {
-        uint32_t r[64];
+template <int N>
+__device__ __forceinline__ void store_cols(uint32_t taddr, const float (&o)[N]) {
+    uint32_t r[N];
 #pragma unroll
-        for (int i = 0; i < 64; ++i) r[i] = __float_as_uint(o[i]);
+    for (int i = 0; i < N; ++i) r[i] = __float_as_uint(o[i]);
+    if constexpr (N == 64) {
         tmem_st_x64(taddr, r);
-    } else if constexpr (D == 32) {
-        uint32_t r[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(o[i]);
+    } else if constexpr (N == 32) {
         tmem_st_x32(taddr, r);
     } else {
-        uint32_t r[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(o[i]);
+        static_assert(N == 16, "column count");
         tmem_st_x16(taddr, r);
     }
 }
 
-template <int D>
-__device__ __forceinline__ void write_o_global(const FlashParams &p, const Work &wk, int row, const float (&o)[D],
+// Writes O[row][0 .. N) = o / l (f32 or f16, vector stores when aligned).
+template <int N>
+__device__ __forceinline__ void write_o_global(const FlashParams &p, const Work &wk, int row, const float (&o)[N],
                                                float l) {
     if (p.o_f16) {
         __half *orow = reinterpret_cast<__half *>(p.o) + wk.slice * p.o_stride + static_cast<long long>(row) * p.o_row;
         if (p.o_vec) {
 #pragma unroll
-            for (int c = 0; c < D; c += 8) {
+            for (int c = 0; c < N; c += 8) {
                 uint4 v;
                 v.x = pack_f16x2(o[c + 0] / l, o[c + 1] / l);
                 v.y = pack_f16x2(o[c + 2] / l, o[c + 3] / l);
@@ -436,40 +453,78 @@ __device__ __forceinline__ void write_o_global(const FlashParams &p, const Work 
             }
         } else {
 #pragma unroll
-            for (int c = 0; c < D; ++c) orow[c] = __float2half_rn(o[c] / l);
+            for (int c = 0; c < N; ++c) orow[c] = __float2half_rn(o[c] / l);
         }
     } else {
         float *orow = reinterpret_cast<float *>(p.o) + wk.slice * p.o_stride + static_cast<long long>(row) * p.o_row;
         if (p.o_vec) {
 #pragma unroll
-            for (int c = 0; c < D; c += 4)
+            for (int c = 0; c < N; c += 4)
                 *reinterpret_cast<float4 *>(orow + c) = make_float4(o[c] / l, o[c + 1] / l, o[c + 2] / l, o[c + 3] / l);
         } else {
 #pragma unroll
-            for (int c = 0; c < D; ++c) orow[c] = o[c] / l;
+            for (int c = 0; c < N; ++c) orow[c] = o[c] / l;
         }
     }
+}
+
+// Row max of kBlockN scores with 8 independent chains: chain i covers x[i], x[8+i], ...
+__device__ __forceinline__ float row_max(const float (&x)[kBlockN]) {
+    static_assert(kBlockN % 16 == 0, "tile width");
+    float mx[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) mx[i] = fmaxf(x[i], x[8 + i]);
+#pragma unroll
+    for (int c = 16; c + 16 <= kBlockN; c += 16) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx[i] = fmax3(mx[i], x[c + i], x[c + 8 + i]);
+    }
+    return fmaxf(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], fmax3(mx[5], mx[6], mx[7])));
+}
+
+// Exponentiates one score row in place against base m (log2 domain), packs P
+// to f16 pairs (rounded as src/flash_h64_bn32.zig:185) and sums the unrounded
+// values in four independent chains.
+__device__ __forceinline__ float exp_row(float (&x)[kBlockN], float kmul, float m, uint32_t (&pk)[kBlockN / 2]) {
+    const uint64_t kmul2 = pack_f32x2(kmul, kmul), negm2 = pack_f32x2(-m, -m);
+    uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};  // (0.0f, 0.0f) x 4
+#pragma unroll
+    for (int c = 0; c < kBlockN / 2; ++c) {
+        float e0, e1, p0, p1;
+        unpack_f32x2(ffma2(pack_f32x2(x[2 * c], x[2 * c + 1]), kmul2, negm2), e0, e1);
+        if (kExp2EmuPeriod > 0 && c % kExp2EmuPeriod >= kExp2EmuPeriod - kExp2EmuCount) {
+            exp2_poly_x2(e0, e1, p0, p1);  // FMA pipe
+        } else {
+            p0 = ex2_approx(e0);  // MUFU
+            p1 = ex2_approx(e1);
+        }
+        sum2[c & 3] = fadd2(sum2[c & 3], pack_f32x2(p0, p1));
+        pk[c] = pack_f16x2(p0, p1);
+    }
+    float s0, s1;
+    unpack_f32x2(fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3])), s0, s1);
+    return s0 + s1;
 }
 
 template <int D>
 __device__ __forceinline__ void softmax_role(const FlashParams &p, uint32_t sbase, uint32_t tmem, const Work &wk,
                                              volatile uint32_t *abort_flag, int warp, int lane) {
     const Bars<D> b{sbase};
-    const int w = (warp - 4) >> 2;                         // Q tile of this warpgroup
+    const int w = (warp - 4) >> 2;                                // Q tile of this warpgroup
+    const int sub = warp & 3;                                     // SM sub-partition
     const int r = static_cast<int>(threadIdx.x) - 128 * (w + 1);  // row inside the tile = TMEM lane
-    const uint32_t lane_field = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t tS = tmem + lane_field + w * 256;
-    const uint32_t tP = tS + 128;
-    const uint32_t tO = tS + 192;
+    const uint32_t tS = tmem + (static_cast<uint32_t>(sub * 32) << 16) + w * kTileCols;
+    const uint32_t tP = tS + kColP, tO = tS + kColO;
     const int n = wk.n[w];
+    const int n_other = wk.n[w ^ 1];
     const int row = wk.q_base + w * kBlockM + r;
     const int seq_len = p.seq_len;
-    // Fast path (scale > 0): mask raw scores, exponent = fma(s, scale*log2e, -m).
+    // scale > 0: mask raw scores, exponent = fma(s, scale*log2e, -m).
     // Otherwise scale first, then mask, exponent = fma(x, 1, -m).
     const bool pre_scale = !(p.scale_log2 > 0.0f);
     const float kmul = pre_scale ? 1.0f : p.scale_log2;
 
-    float m = -INFINITY;  // running max of scaled scores, log2 domain (stale by < 8)
+    float m = -INFINITY;  // exponent base: scaled row max, log2 domain (stale by < 8)
     float l = 0.0f;       // running sum of 2^(x - m)
     bool ok = true;
     for (int j = 0; j < n; ++j) {
@@ -492,7 +547,8 @@ __device__ __forceinline__ void softmax_role(const FlashParams &p, uint32_t sbas
             for (int c = 0; c < kBlockN; ++c) x[c] *= p.scale_log2;
         }
         // masking (reference: src/flash_h64_bn32.zig:122-135): keys >= seq_len and,
-        // under causal masking, keys > row.  Only the last K tile of a Q tile can hold them.
+        // under causal masking, keys > row.  Only the last K tile of a Q tile holds
+        // either: a Q tile's rows share one 128-key tile index.
         if (j == n - 1) {
             int lim = seq_len - j * kBlockN;
             if (p.causal) lim = min(lim, row - j * kBlockN + 1);
@@ -501,75 +557,39 @@ __device__ __forceinline__ void softmax_role(const FlashParams &p, uint32_t sbas
                 for (int c = 0; c < kBlockN; ++c) x[c] = c < lim ? x[c] : -INFINITY;
             }
         }
-        // row max: 8 independent 3-input max chains (short dependency chains)
-        // chain i covers x[i], x[8+i], ..., x[120+i]
-        static_assert(kBlockN % 16 == 8 || kBlockN % 16 == 0, "tile width");
-        float mx[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) mx[i] = x[i];
-#pragma unroll
-        for (int c = 8; c + 16 <= kBlockN; c += 16) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) mx[i] = fmax3(mx[i], x[c + i], x[c + 8 + i]);
-        }
-        if constexpr (kBlockN % 16 == 0) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) mx[i] = fmaxf(mx[i], x[kBlockN - 8 + i]);
-        }
-        const float m_tile = fmaxf(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], fmax3(mx[5], mx[6], mx[7]))) * kmul;
-        const float m_new = fmaxf(m, m_tile);
+        const float m_new = fmaxf(m, row_max(x) * kmul);
         const bool need = m_new > m + kRescaleThreshold;
         float m_use = need ? m_new : m;
         m_use = m_use == -INFINITY ? 0.0f : m_use;  // row with nothing visible yet
         const float alpha = ex2_approx(m - m_use);  // 1 when not rescaling, 0 on the first tile
-        const float neg_m = -m_use;
 
-        // Exp phase.  Warps 4+i (tile 0) and 8+i (tile 1) share SM sub-partition i and
-        // its MUFU unit; they take turns (tile j of warp 4+i, tile j of warp 8+i, tile
-        // j+1 of warp 4+i, ...) so one runs its exponentials while the other loads S,
-        // reduces the max and stores P.
-        const int n_other = wk.n[w ^ 1];
-        const int sub = warp & 3;
+        // The two softmax warps of a sub-partition (Q tiles 0 and 1) share its MUFU
+        // unit; optionally they take turns: tile j of Q tile 0, tile j of Q tile 1, ...
         if (kExpTurns && (w == 0 ? (j >= 1 && j - 1 < n_other) : (j < n_other))) {
             ok = warp_wait(b.turn(sub, w), (w == 0 ? j - 1 : j) & 1, abort_flag, kSiteTurn);
             if (!ok) break;
         }
         uint32_t pk[kBlockN / 2];
-        uint64_t sum2 = 0ull;  // (0.0f, 0.0f)
-        const uint64_t kmul2 = pack_f32x2(kmul, kmul), negm2 = pack_f32x2(neg_m, neg_m);
-#pragma unroll
-        for (int c = 0; c < kBlockN / 2; ++c) {
-            float e0, e1, p0, p1;
-            unpack_f32x2(ffma2(pack_f32x2(x[2 * c], x[2 * c + 1]), kmul2, negm2), e0, e1);
-            if (kExp2EmuPeriod > 0 && c % kExp2EmuPeriod >= kExp2EmuPeriod - kExp2EmuCount) {
-                exp2_poly_x2(e0, e1, p0, p1);  // FMA pipe
-            } else {
-                p0 = ex2_approx(e0);  // MUFU
-                p1 = ex2_approx(e1);
-            }
-            const uint64_t pp = pack_f32x2(p0, p1);
-            sum2 = fadd2(sum2, pp);
-            pk[c] = pack_f16x2(p0, p1);  // P rounded to f16 (as src/flash_h64_bn32.zig:185)
-        }
-        __syncwarp();
+        const float tsum = exp_row(x, kmul, m_use, pk);
         if (kExpTurns && (w == 0 ? (j < n_other) : (j + 1 < n_other))) {
+            __syncwarp();
             if (lane == 0) mbar_arrive(b.turn(sub, w ^ 1));
         }
-        float s0, s1;
-        unpack_f32x2(sum2, s0, s1);
-        l = l * alpha + (s0 + s1);
+        l = l * alpha + tsum;
+        m = m_use;
 
         if (j > 0) {
-            // PV of the previous tile must be done: it reads P and accumulates into O.
+            // PV(j-1) reads P and accumulates into O: it must be done before P is
+            // overwritten and before O is rebased.
             ok = warp_wait(b.o_done(w), (j - 1) & 1, abort_flag, kSiteODone);
             if (!ok) break;
             tc_fence_after();
             if (__any_sync(0xffffffffu, need)) {
                 float o[D];
-                load_o_row<D>(tO, o);
+                load_cols<D>(tO, o);
 #pragma unroll
                 for (int c = 0; c < D; ++c) o[c] *= alpha;
-                store_o_row<D>(tO, o);
+                store_cols<D>(tO, o);
             }
         }
         tmem_st_x64(tP, pk);
@@ -577,7 +597,6 @@ __device__ __forceinline__ void softmax_role(const FlashParams &p, uint32_t sbas
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(b.p_full(w));
-        m = m_use;
     }
 
     if (ok && n > 0) {
@@ -585,7 +604,7 @@ __device__ __forceinline__ void softmax_role(const FlashParams &p, uint32_t sbas
         if (ok) {
             tc_fence_after();
             float o[D];
-            load_o_row<D>(tO, o);
+            load_cols<D>(tO, o);
             if (row < seq_len) write_o_global<D>(p, wk, row, o, l);
         }
     }
@@ -613,16 +632,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int s = 0; s < L::kStages; ++s) {
             mbar_init(b.k_full(s), 1);
             mbar_init(b.v_full(s), 1);
-            mbar_init(b.kv_empty(s), 1);
+            mbar_init(b.kv_empty(s), kQTiles);  // one arrival per MMA warp
         }
         for (int w = 0; w < kQTiles; ++w) {
             mbar_init(b.s_full(w), 1);
             mbar_init(b.s_free(w), 4);  // one arrival per softmax warp
             mbar_init(b.p_full(w), 4);
             mbar_init(b.o_done(w), 1);
+            mbar_init(b.drain(w), 1);
         }
-        mbar_init(b.drain(), 1);
-        for (int i = 0; i < 8; ++i) mbar_init(b.at(L::kBarTurn + i), 1);
+        for (int i = 0; i < 4 * kQTiles; ++i) mbar_init(b.at(L::kBarTurn + i), 1);
         *abort_flag = 0u;
         mbar_fence_init();
     }
@@ -647,8 +666,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             producer_lsu<D>(p, smem, sbase, wk, abort_flag, lane);
         }
         __syncwarp();
-    } else if (warp == 1) {
-        mma_role<D>(sbase, tmem, wk, abort_flag);
+    } else if (warp == 1 || warp == 2) {
+        mma_role<D>(warp - 1, sbase, tmem, wk, abort_flag, lane);
     } else if (warp >= 4) {
         softmax_role<D>(p, sbase, tmem, wk, abort_flag, warp, lane);
     }

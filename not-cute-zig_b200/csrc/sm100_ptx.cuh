@@ -55,6 +55,14 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
     return t;
 }
 
+// SM cycle counter: cheap to read (the chip-wide %globaltimer is not), used
+// to bound spin-waits.
+__device__ __forceinline__ uint64_t sm_clock() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%clock64;" : "=l"(t));
+    return t;
+}
+
 // --------------------------------------------------------------------------
 // mbarrier
 // --------------------------------------------------------------------------
@@ -199,6 +207,74 @@ __device__ __forceinline__ void umma_ts_elect(uint32_t d_tmem, uint32_t a_tmem, 
         "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
+// S = Q K^T over head_dim: kSteps SS MMAs along K (descriptors advance by 32 bytes
+// = 2 in the encoded start address), first one overwrites D.
+template <int kSteps>
+__device__ __forceinline__ void umma_ss_chain_elect(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc) {
+    static_assert(kSteps >= 1 && kSteps <= 4, "K steps");
+    const uint64_t a1 = a_desc + 2, a2 = a_desc + 4, a3 = a_desc + 6;
+    const uint64_t b1 = b_desc + 2, b2 = b_desc + 4, b3 = b_desc + 6;
+    if constexpr (kSteps == 1) {
+        asm volatile(
+            "{\n.reg .pred e;\nelect.sync _|e, -1;\n"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, 0;\n}\n" ::"r"(d_tmem),
+            "l"(a_desc), "l"(b_desc), "r"(idesc)
+            : "memory");
+    } else if constexpr (kSteps == 2) {
+        asm volatile(
+            "{\n.reg .pred e;\nelect.sync _|e, -1;\n"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, 0;\n"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %4, %5, %3, 1;\n}\n" ::"r"(d_tmem),
+            "l"(a_desc), "l"(b_desc), "r"(idesc), "l"(a1), "l"(b1)
+            : "memory");
+    } else {
+        asm volatile(
+            "{\n.reg .pred e;\nelect.sync _|e, -1;\n"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, 0;\n"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %4, %5, %3, 1;\n"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %6, %7, %3, 1;\n"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %8, %9, %3, 1;\n}\n" ::"r"(d_tmem),
+            "l"(a_desc), "l"(b_desc), "r"(idesc), "l"(a1), "l"(b1), "l"(a2), "l"(b2), "l"(a3), "l"(b3)
+            : "memory");
+    }
+}
+// O (+)= P V over kSteps key steps: A = P from TMEM (8 columns per step), B = V
+// descriptor advancing by `b_step` (encoded units) per step.  `accumulate`
+// applies to the first step; later steps always accumulate.
+template <int kSteps>
+__device__ __forceinline__ void umma_ts_chain_elect(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                                   uint64_t b_step, uint32_t idesc, uint32_t accumulate) {
+    static_assert(kSteps == 4 || kSteps == 8, "key steps");
+    uint64_t b[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) b[i] = b_desc + b_step * i;
+    if constexpr (kSteps == 4) {
+        asm volatile(
+            "{\n.reg .pred p, e;\nelect.sync _|e, -1;\nsetp.ne.b32 p, %3, 0;\n"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %4, %2, p;\n"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%5], %6, %2, 1;\n"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%7], %8, %2, 1;\n"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%9], %10, %2, 1;\n}\n" ::"r"(d_tmem),
+            "r"(a_tmem), "r"(idesc), "r"(accumulate), "l"(b[0]), "r"(a_tmem + 8), "l"(b[1]), "r"(a_tmem + 16),
+            "l"(b[2]), "r"(a_tmem + 24), "l"(b[3])
+            : "memory");
+    } else {
+        asm volatile(
+            "{\n.reg .pred p, e;\nelect.sync _|e, -1;\nsetp.ne.b32 p, %3, 0;\n"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %4, %2, p;\n"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%5], %6, %2, 1;\n"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%7], %8, %2, 1;\n"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%9], %10, %2, 1;\n"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%11], %12, %2, 1;\n"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%13], %14, %2, 1;\n"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%15], %16, %2, 1;\n"
+            "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%17], %18, %2, 1;\n}\n" ::"r"(d_tmem),
+            "r"(a_tmem), "r"(idesc), "r"(accumulate), "l"(b[0]), "r"(a_tmem + 8), "l"(b[1]), "r"(a_tmem + 16),
+            "l"(b[2]), "r"(a_tmem + 24), "l"(b[3]), "r"(a_tmem + 32), "l"(b[4]), "r"(a_tmem + 40), "l"(b[5]),
+            "r"(a_tmem + 48), "l"(b[6]), "r"(a_tmem + 56), "l"(b[7])
+            : "memory");
+    }
+}
 __device__ __forceinline__ void umma_commit_elect(uint32_t bar) {
     asm volatile(
         "{\n"
@@ -295,6 +371,51 @@ __device__ __forceinline__ void tmem_st_x64(uint32_t taddr, const uint32_t (&r)[
         :
         : "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31]), "r"(r[32]), "r"(r[33]), "r"(r[34]), "r"(r[35]), "r"(r[36]), "r"(r[37]), "r"(r[38]), "r"(r[39]), "r"(r[40]), "r"(r[41]), "r"(r[42]), "r"(r[43]), "r"(r[44]), "r"(r[45]), "r"(r[46]), "r"(r[47]), "r"(r[48]), "r"(r[49]), "r"(r[50]), "r"(r[51]), "r"(r[52]), "r"(r[53]), "r"(r[54]), "r"(r[55]), "r"(r[56]), "r"(r[57]), "r"(r[58]), "r"(r[59]), "r"(r[60]), "r"(r[61]), "r"(r[62]), "r"(r[63])
         : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_x8_wait(uint32_t taddr, uint32_t (&r)[8]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];\n"
+        "tcgen05.wait::ld.sync.aligned;\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+        : "r"(taddr)
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_x8(uint32_t taddr, const uint32_t (&r)[8]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};\n"
+        :
+        : "r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_x32_async(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+}
+
+// Waits for the asynchronous loads of a and b; both arrays are in/out operands,
+// so no use of them can be scheduled before the wait.
+__device__ __forceinline__ void tmem_wait_ld_2x32(uint32_t (&a)[32], uint32_t (&b)[32]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n" : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]), "+r"(a[6]), "+r"(a[7]), "+r"(a[8]), "+r"(a[9]), "+r"(a[10]), "+r"(a[11]), "+r"(a[12]), "+r"(a[13]), "+r"(a[14]), "+r"(a[15]), "+r"(a[16]), "+r"(a[17]), "+r"(a[18]), "+r"(a[19]), "+r"(a[20]), "+r"(a[21]), "+r"(a[22]), "+r"(a[23]), "+r"(a[24]), "+r"(a[25]), "+r"(a[26]), "+r"(a[27]), "+r"(a[28]), "+r"(a[29]), "+r"(a[30]), "+r"(a[31]), "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3]), "+r"(b[4]), "+r"(b[5]), "+r"(b[6]), "+r"(b[7]), "+r"(b[8]), "+r"(b[9]), "+r"(b[10]), "+r"(b[11]), "+r"(b[12]), "+r"(b[13]), "+r"(b[14]), "+r"(b[15]), "+r"(b[16]), "+r"(b[17]), "+r"(b[18]), "+r"(b[19]), "+r"(b[20]), "+r"(b[21]), "+r"(b[22]), "+r"(b[23]), "+r"(b[24]), "+r"(b[25]), "+r"(b[26]), "+r"(b[27]), "+r"(b[28]), "+r"(b[29]), "+r"(b[30]), "+r"(b[31]) : : "memory");
+}
+
+// Asynchronous form: the registers are written when tcgen05.wait::ld
+// completes; tmem_wait_ld_x64 takes them as in/out operands so no use can be
+// scheduled before the wait.
+__device__ __forceinline__ void tmem_ld_x64_async(uint32_t taddr, uint32_t (&r)[64]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];\n"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+        : "r"(taddr)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld_x64(uint32_t (&r)[64]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n" : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31]), "+r"(r[32]), "+r"(r[33]), "+r"(r[34]), "+r"(r[35]), "+r"(r[36]), "+r"(r[37]), "+r"(r[38]), "+r"(r[39]), "+r"(r[40]), "+r"(r[41]), "+r"(r[42]), "+r"(r[43]), "+r"(r[44]), "+r"(r[45]), "+r"(r[46]), "+r"(r[47]), "+r"(r[48]), "+r"(r[49]), "+r"(r[50]), "+r"(r[51]), "+r"(r[52]), "+r"(r[53]), "+r"(r[54]), "+r"(r[55]), "+r"(r[56]), "+r"(r[57]), "+r"(r[58]), "+r"(r[59]), "+r"(r[60]), "+r"(r[61]), "+r"(r[62]), "+r"(r[63]) : : "memory");
 }
 
 // --------------------------------------------------------------------------
