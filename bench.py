@@ -308,7 +308,8 @@ def main():
     per_gpu = step_flops / (ms_step / 1e3) / 1e12
     assert np.isfinite(o[: s * d].float().cpu().numpy()).all()
 
-    # e2e through the C ABI (flash.launch) with pinned host buffers
+    # e2e through the C ABI with pinned host buffers: ncz_flash_fwd_host uploads
+    # Q/K/V, runs the forward and downloads O in slice chunks on three streams.
     e2e = None
     if not args.no_e2e:
         pq, pk_, pv = (torch.from_numpy(a).pin_memory() for a in (hq, hk, hv))
@@ -316,11 +317,7 @@ def main():
         dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
 
         def e2e_step():
-            dq.copy_(pq, non_blocking=True)
-            dk.copy_(pk_, non_blocking=True)
-            dv.copy_(pv, non_blocking=True)
-            ncz.launch(dq, dk, dv, o, opts, stream=stream)
-            po.copy_(o, non_blocking=True)
+            ncz.launch_host(pq, pk_, pv, po, dq, dk, dv, o, opts, stream=stream)
 
         for _ in range(3):
             e2e_step()
@@ -336,7 +333,7 @@ def main():
             dist.all_reduce(et, op=dist.ReduceOp.MAX)
         e2e = {"value": world * step_flops * args.e2e_steps / (float(et.item()) / 1e3) / 1e12, "unit": "TFLOP/s",
                "h2d_bytes_per_step": 3 * n * 2, "d2h_bytes_per_step": n * 4, "steps": args.e2e_steps,
-               "api": "flash.launch -> ncz_flash_launch (C ABI)"}
+               "api": "flash.launch_host -> ncz_flash_fwd_host (C ABI), default chunking"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:

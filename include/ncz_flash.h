@@ -133,6 +133,20 @@ int ncz_flash_fwd_ex(const ncz_flash_desc *desc);
  * (src/cuda.zig:181-196); this replaces a per-device loop over flash.launch. */
 int ncz_flash_fwd_multi(const ncz_flash_desc *descs, int count);
 
+/* Host-buffer forward with overlapped copies.  q_host, k_host, v_host and
+ * o_host are HOST buffers laid out exactly like desc->q/k/v/o (same strides);
+ * desc->q/k/v/o are caller-owned device buffers of the same layout that stage
+ * them.  Slices are processed in chunks of chunk_slices (0 = bh/8 rounded up):
+ * a chunk's Q/K/V upload, its forward and its O download run on separate
+ * streams, so the upload of chunk i+1 overlaps the forward of chunk i and the
+ * download of chunk i-1.  Host buffers must be page-locked (pinned) for the
+ * copies to run asynchronously.  Everything is ordered on desc->stream: work
+ * enqueued on it afterwards runs once O is in host memory.  Replaces the
+ * upload / flash.launch / download sequence of the reference's callers
+ * (src/main.zig:254-271). */
+int ncz_flash_fwd_host(const ncz_flash_desc *desc, const void *q_host, const void *k_host,
+                       const void *v_host, void *o_host, size_t chunk_slices);
+
 /* Synchronises `stream` (on `device`, -1 = current), then reads and clears the
  * device's in-kernel status word.  Returns NCZ_ERROR_DEVICE_TIMEOUT when a
  * bounded wait expired in a kernel since the last call, a CUDA error code

@@ -9,6 +9,7 @@ from .flash import (  # noqa: F401
     Options,
     launch,
     launch_ex,
+    launch_host,
     launch_multi,
     select_kernel,
     sync_status,

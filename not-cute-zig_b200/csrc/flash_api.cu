@@ -245,6 +245,85 @@ Resolved reference_args(const void *q, const void *k, const void *v, void *o, si
     return from_desc(desc);
 }
 
+// Per-device streams and events of the host-buffer pipeline (library-owned,
+// created on first use).  `mu` serialises callers on one device: the events
+// are re-recorded per chunk and waited on right away, which is only ordered
+// within one caller's enqueue sequence.
+struct HostPipe {
+    std::mutex mu;
+    bool ready = false;
+    cudaStream_t up = nullptr, down = nullptr;
+    cudaEvent_t fork = nullptr, in_ready = nullptr, out_ready = nullptr, join = nullptr;
+};
+HostPipe g_pipes[kMaxDevices];
+
+int pipe_setup(HostPipe &hp) {
+    if (hp.ready) return NCZ_SUCCESS;
+    cudaError_t e = cudaStreamCreateWithFlags(&hp.up, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&hp.down, cudaStreamNonBlocking);
+    cudaEvent_t *evs[4] = {&hp.fork, &hp.in_ready, &hp.out_ready, &hp.join};
+    for (int i = 0; i < 4 && e == cudaSuccess; ++i) e = cudaEventCreateWithFlags(evs[i], cudaEventDisableTiming);
+    if (e != cudaSuccess) return map_cuda_error(e);
+    hp.ready = true;
+    return NCZ_SUCCESS;
+}
+
+// Elements the slices [s0, s1) of one operand occupy: whole strides for all but
+// the last slice, which ends at its last row's last element.
+size_t chunk_elems(size_t s0, size_t s1, size_t slice, size_t row, size_t seq, size_t d) {
+    return (s1 - s0 - 1) * slice + (seq - 1) * row + d;
+}
+
+int host_pipeline(const Resolved &r, const void *qh, const void *kh, const void *vh, void *oh, size_t chunk,
+                  int dev) {
+    HostPipe &hp = g_pipes[dev];
+    std::lock_guard<std::mutex> lock(hp.mu);
+    int st = pipe_setup(hp);
+    if (st != NCZ_SUCCESS) return st;
+    const size_t osz = r.o_dtype == NCZ_DTYPE_F16 ? 2 : 4;
+    cudaError_t e = cudaEventRecord(hp.fork, r.stream);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(hp.up, hp.fork, 0);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(hp.down, hp.fork, 0);
+    if (e != cudaSuccess) return map_cuda_error(e);
+    for (size_t s0 = 0; s0 < r.bh; s0 += chunk) {
+        const size_t s1 = s0 + chunk < r.bh ? s0 + chunk : r.bh;
+        struct Op {
+            const void *dev;
+            const void *host;
+            size_t slice, row;
+        } in[3] = {{r.q, qh, r.qs, r.qr}, {r.k, kh, r.ks, r.kr}, {r.v, vh, r.vs, r.vr}};
+        for (int i = 0; i < 3 && e == cudaSuccess; ++i) {
+            const size_t off = s0 * in[i].slice * 2;
+            e = cudaMemcpyAsync(static_cast<char *>(const_cast<void *>(in[i].dev)) + off,
+                                static_cast<const char *>(in[i].host) + off,
+                                chunk_elems(s0, s1, in[i].slice, in[i].row, r.seq, r.d) * 2, cudaMemcpyHostToDevice,
+                                hp.up);
+        }
+        if (e == cudaSuccess) e = cudaEventRecord(hp.in_ready, hp.up);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(r.stream, hp.in_ready, 0);
+        if (e != cudaSuccess) return map_cuda_error(e);
+        Resolved rc = r;
+        rc.q = static_cast<const char *>(r.q) + s0 * r.qs * 2;
+        rc.k = static_cast<const char *>(r.k) + s0 * r.ks * 2;
+        rc.v = static_cast<const char *>(r.v) + s0 * r.vs * 2;
+        rc.o = static_cast<char *>(r.o) + s0 * r.os * osz;
+        rc.bh = s1 - s0;
+        st = launch_on_current(rc, dev);
+        if (st != NCZ_SUCCESS) return st;
+        e = cudaEventRecord(hp.out_ready, r.stream);
+        if (e == cudaSuccess) e = cudaStreamWaitEvent(hp.down, hp.out_ready, 0);
+        if (e == cudaSuccess) {
+            const size_t off = s0 * r.os * osz;
+            e = cudaMemcpyAsync(static_cast<char *>(oh) + off, static_cast<const char *>(r.o) + off,
+                                chunk_elems(s0, s1, r.os, r.orow, r.seq, r.d) * osz, cudaMemcpyDeviceToHost, hp.down);
+        }
+        if (e != cudaSuccess) return map_cuda_error(e);
+    }
+    e = cudaEventRecord(hp.join, hp.down);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(r.stream, hp.join, 0);
+    return e == cudaSuccess ? NCZ_SUCCESS : map_cuda_error(e);
+}
+
 }  // namespace
 
 extern "C" {
@@ -358,6 +437,31 @@ int ncz_flash_fwd_multi(const ncz_flash_desc *descs, int count) {
         if (st != NCZ_SUCCESS) return st;
     }
     return NCZ_SUCCESS;
+}
+
+int ncz_flash_fwd_host(const ncz_flash_desc *desc, const void *q_host, const void *k_host, const void *v_host,
+                       void *o_host, size_t chunk_slices) {
+    if (desc == nullptr || q_host == nullptr || k_host == nullptr || v_host == nullptr || o_host == nullptr)
+        return NCZ_ERROR_INVALID_VALUE;
+    const Resolved r = from_desc(*desc);
+    int st = validate_resolved(r);
+    if (st != NCZ_SUCCESS) return st;
+    st = ncz_init();
+    if (st != NCZ_SUCCESS) return st;
+    int prev = 0;
+    cudaError_t e = cudaGetDevice(&prev);
+    if (e != cudaSuccess) return map_cuda_error(e);
+    const int dev = r.device >= 0 ? r.device : prev;
+    if (dev >= kMaxDevices) return NCZ_ERROR_INVALID_DEVICE;
+    if (dev != prev) {
+        e = cudaSetDevice(dev);
+        if (e != cudaSuccess) return map_cuda_error(e);
+    }
+    // Default: 8 chunks, so one chunk's upload hides the previous chunk's forward.
+    const size_t chunk = chunk_slices > 0 ? chunk_slices : (r.bh + 7) / 8;
+    st = host_pipeline(r, q_host, k_host, v_host, o_host, chunk, dev);
+    if (dev != prev) cudaSetDevice(prev);
+    return st;
 }
 
 int ncz_flash_sync_status(int device, void *stream, uint32_t *detail) {

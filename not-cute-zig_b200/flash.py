@@ -107,6 +107,7 @@ _SIGNATURES = {
     ),
     "ncz_flash_fwd_ex": (ctypes.c_int, [ctypes.POINTER(_Desc)]),
     "ncz_flash_fwd_multi": (ctypes.c_int, [ctypes.POINTER(_Desc), ctypes.c_int]),
+    "ncz_flash_fwd_host": (ctypes.c_int, [ctypes.POINTER(_Desc), _VP, _VP, _VP, _VP, _SZ]),
     "ncz_flash_sync_status": (ctypes.c_int, [ctypes.c_int, _VP, ctypes.POINTER(ctypes.c_uint32)]),
     "ncz_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "ncz_launch_count": (ctypes.c_uint64, []),
@@ -266,6 +267,23 @@ def launch_ex(q, k, v, o, opts: Options, *, row_strides: Optional[Sequence[int]]
     """ncz_flash_fwd_ex: the reference launch plus the layout extensions."""
     d = make_desc(q, k, v, o, opts, row_strides=row_strides, producer=producer, device=device, stream=stream)
     _check(lib().ncz_flash_fwd_ex(ctypes.byref(d)), "flash.launch_ex")
+
+
+def launch_host(q_host, k_host, v_host, o_host, q, k, v, o, opts: Options, *, chunk_slices: int = 0,
+                row_strides: Optional[Sequence[int]] = None, producer: str = "auto", stream=None) -> None:
+    """ncz_flash_fwd_host: forward on HOST buffers (q_host .. o_host, CPU tensors,
+    pinned for overlap) staged through the device buffers q .. o of the same
+    layout; uploads, forwards and downloads are pipelined in chunks of
+    chunk_slices slices (0 = automatic).  O is in o_host once `stream` reaches
+    the point after this call (e.g. after stream.synchronize())."""
+    d = make_desc(q, k, v, o, opts, row_strides=row_strides, producer=producer, stream=stream)
+    for h, t, name in ((q_host, q, "q"), (k_host, k, "k"), (v_host, v, "v"), (o_host, o, "o")):
+        if h.device.type != "cpu":
+            raise FlashError(5, f"{name}_host must be a host (CPU) tensor")
+        if h.dtype != t.dtype or h.numel() < t.numel() or not h.is_contiguous():
+            raise FlashError(5, f"{name}_host must be a contiguous {t.dtype} tensor of >= {t.numel()} elements")
+    _check(lib().ncz_flash_fwd_host(ctypes.byref(d), q_host.data_ptr(), k_host.data_ptr(), v_host.data_ptr(),
+                                    o_host.data_ptr(), int(chunk_slices)), "flash.launch_host")
 
 
 def launch_multi(descs: Sequence[_Desc]) -> None:

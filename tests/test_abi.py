@@ -210,3 +210,23 @@ def test_shard_ranges(ncz):
             assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
             sizes = [hi - lo for lo, hi in ranges]
             assert max(sizes) - min(sizes) <= 1
+
+
+def test_host_pipeline_validates_before_any_device_work(ncz):
+    """ncz_flash_fwd_host: null host buffers and invalid shapes are rejected
+    before the library touches a device; with no device it fails loudly."""
+    import torch
+
+    lib = ncz.flash.lib()
+    D = ncz.flash._Desc
+    st = 64 * 16
+    good = D(q=1, k=1, v=1, o=1, batch_heads=2, seq_len=64, head_dim=16, q_stride=st, k_stride=st, v_stride=st,
+             o_stride=st, scale=0.25, causal=1, o_dtype=0, producer=0, device=-1, stream=None)
+    assert ncz.flash.STATUS_NAMES[lib.ncz_flash_fwd_host(ctypes.byref(good), None, 1, 1, 1, 0)] == "InvalidValue"
+    assert ncz.flash.STATUS_NAMES[lib.ncz_flash_fwd_host(None, 1, 1, 1, 1, 0)] == "InvalidValue"
+    bad = D.from_buffer_copy(good)
+    bad.head_dim = 48
+    assert ncz.flash.STATUS_NAMES[lib.ncz_flash_fwd_host(ctypes.byref(bad), 1, 1, 1, 1, 0)] == "InvalidValue"
+    if not torch.cuda.is_available():
+        rc = lib.ncz_flash_fwd_host(ctypes.byref(good), 1, 1, 1, 1, 0)
+        assert ncz.flash.STATUS_NAMES[rc] in ("NoDevice", "NotInitialized", "NotFound", "UnknownError")

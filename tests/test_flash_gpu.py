@@ -218,3 +218,37 @@ def test_repeated_launches_are_bit_identical(ncz, oracle_mod, d):
         for _ in range(3):
             assert np.array_equal(run(ncz, p, producer=producer), first)
     assert np.array_equal(run(ncz, p, producer="tma"), run(ncz, p, producer="lsu"))
+
+
+@pytest.mark.parametrize("chunk", [0, 1, 3, 7, 64])
+@pytest.mark.parametrize("o_dtype", ["float32", "float16"])
+def test_host_pipeline_matches_device_launch(ncz, oracle_mod, chunk, o_dtype):
+    """ncz_flash_fwd_host (chunked upload / forward / download on three streams)
+    gives exactly the device-path result, for chunk sizes that do and do not
+    divide batch_heads, with padded slice strides (the last chunk copies only up
+    to its last row)."""
+    bh, s, d = 7, 333, 64
+    strides = (s * d + 24, s * d + 40, s * d + 8, s * d + 16)
+    p = C.normal_problem(bh, s, d, True, 61, oracle_mod, std=0.7, strides=strides)
+    dev = torch.device("cuda:0")
+    q, k, v = (torch.from_numpy(a).to(dev) for a in (p.q, p.k, p.v))
+    o_ref = torch.full((bh * strides[3],), SENTINEL, dtype=getattr(torch, o_dtype), device=dev)
+    opts = ncz.Options(seq_len=s, head_dim=d, q_stride=strides[0], k_stride=strides[1], v_stride=strides[2],
+                       o_stride=strides[3], scale=p.scale, batch_heads=bh, causal=True)
+    ncz.launch_ex(q, k, v, o_ref, opts)
+    assert ncz.sync_status() == 0
+    want = o_ref.cpu()
+
+    qh, kh, vh = (torch.from_numpy(a).pin_memory() for a in (p.q, p.k, p.v))
+    oh = torch.full((bh * strides[3],), SENTINEL, dtype=getattr(torch, o_dtype)).pin_memory()
+    qd, kd, vd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    od = torch.full_like(o_ref, SENTINEL)
+    stream = torch.cuda.Stream(dev)
+    ncz.launch_host(qh, kh, vh, oh, qd, kd, vd, od, opts, chunk_slices=chunk, stream=stream)
+    stream.synchronize()
+    assert ncz.sync_status() == 0
+    got = oh.clone()
+    idx = C.active_index(p)
+    ti = torch.from_numpy(idx)
+    assert torch.equal(got[ti], want[ti])
+    C.check(got.float().numpy(), C.reference(p, oracle_mod), idx, f"host pipeline chunk={chunk} {o_dtype}")
