@@ -127,6 +127,16 @@ int ncz_flash_launch(const void *q, size_t q_len, const void *k, size_t k_len, c
  * No reference counterpart beyond flash.launch (src/flash.zig:31-70). */
 int ncz_flash_fwd_ex(const ncz_flash_desc *desc);
 
+/* Extended launch with an explicit split-KV request.  splits = 0 chooses
+ * automatically (what every other launch entry point does: split when the
+ * grid of batch_heads x ceil(seq_len/256) CTAs fills at most half the SMs),
+ * 1 never splits, n > 1 splits each Q group's K tiles into up to min(n, 8) ranges
+ * computed by separate CTAs and merged by a second kernel.  Partial results
+ * live in a library-owned stream-ordered memory pool; nothing is allocated
+ * when no split is made.  The reference has no split path (its grid is
+ * (ceil(S/16), bh), src/flash.zig:45-69). */
+int ncz_flash_fwd_splits(const ncz_flash_desc *desc, int splits);
+
 /* One call, several devices: descs[i] is launched on descs[i].device (each on
  * its own stream); the caller's current device is restored.  Used to shard
  * batch x head slices across GPUs.  The reference has one device only

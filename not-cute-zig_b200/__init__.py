@@ -11,6 +11,7 @@ from .flash import (  # noqa: F401
     launch_ex,
     launch_host,
     launch_multi,
+    launch_splits,
     select_kernel,
     sync_status,
 )

@@ -13,6 +13,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdint>
@@ -74,6 +75,7 @@ struct Resolved {
     int producer;
     int device;
     cudaStream_t stream;
+    int splits = 0;  // split-KV request: 0 = automatic, 1 = none, n = n ranges
 };
 
 bool mul_ok(size_t a, size_t b, size_t *out) { return !__builtin_mul_overflow(a, b, out); }
@@ -99,7 +101,7 @@ int validate_resolved(const Resolved &r) {
     if (r.seq > (size_t(1) << 30)) return NCZ_ERROR_INVALID_VALUE;
     const size_t groups = (r.seq + kGroupRows - 1) / kGroupRows;
     size_t grid;
-    if (!mul_ok(groups, r.bh, &grid) || grid > size_t(0x7FFFFFFF)) return NCZ_ERROR_INVALID_VALUE;
+    if (!mul_ok(groups, r.bh, &grid) || grid > size_t(0x7FFFFFFF) / 8) return NCZ_ERROR_INVALID_VALUE;
     if (r.bh > size_t(0x7FFFFFFF)) return NCZ_ERROR_INVALID_VALUE;
     return NCZ_SUCCESS;
 }
@@ -159,6 +161,73 @@ int launch_variant(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorM
     return NCZ_SUCCESS;
 }
 
+template <int D>
+int launch_combine(const FlashParams &p, cudaStream_t stream) {
+    const long long rows = static_cast<long long>(p.batch_heads) * p.seq_len;
+    const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
+    ncz::combine_splits<D><<<grid, 256, 0, stream>>>(p);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return map_cuda_error(e);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return NCZ_SUCCESS;
+}
+
+// Library-owned stream-ordered memory pool per device for split-KV partials:
+// allocations are ordered on the launch stream, so calls on different streams
+// never share a workspace, and the pool keeps freed memory for the next call.
+cudaMemPool_t g_pool[kMaxDevices];
+int g_num_sms[kMaxDevices];
+
+int device_pool(int dev, cudaMemPool_t *pool) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (g_pool[dev] == nullptr) {
+        cudaMemPoolProps props;
+        std::memset(&props, 0, sizeof(props));
+        props.allocType = cudaMemAllocationTypePinned;
+        props.location.type = cudaMemLocationTypeDevice;
+        props.location.id = dev;
+        cudaError_t e = cudaMemPoolCreate(&g_pool[dev], &props);
+        if (e != cudaSuccess) return map_cuda_error(e);
+        uint64_t keep = uint64_t(1) << 30;  // keep up to 1 GiB between calls
+        e = cudaMemPoolSetAttribute(g_pool[dev], cudaMemPoolAttrReleaseThreshold, &keep);
+        if (e != cudaSuccess) return map_cuda_error(e);
+    }
+    *pool = g_pool[dev];
+    return NCZ_SUCCESS;
+}
+
+int device_sms(int dev) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (g_num_sms[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        g_num_sms[dev] = n;
+    }
+    return g_num_sms[dev];
+}
+
+// Split-KV ranges for a launch.  Automatic: only when the grid fills at most
+// half the SMs and the K range is long (>= 16 tiles; each range keeps >= 4).  A
+// CTA costs about the time of 4-5 K tiles in fixed set-up and hand-off, and the
+// merge is a second launch, so shorter ranges (config 2: 8 tiles) gain nothing.
+void choose_splits(const Resolved &r, int dev, int *splits, int *per_split) {
+    const int n_kv = static_cast<int>((r.seq + ncz::kBlockN - 1) / ncz::kBlockN);
+    const size_t ctas = ((r.seq + kGroupRows - 1) / kGroupRows) * r.bh;
+    int want = r.splits;
+    if (want == 0) {
+        const size_t sms = static_cast<size_t>(device_sms(dev));
+        want = 1;
+        if (ctas * 2 <= sms && n_kv >= 16) {
+            const int by_sms = static_cast<int>((sms + ctas - 1) / ctas);
+            want = std::min(std::min(by_sms, n_kv / 4), ncz::kMaxSplits);
+        }
+    }
+    want = std::max(1, std::min(std::min(want, n_kv), ncz::kMaxSplits));
+    const int per = (n_kv + want - 1) / want;
+    *per_split = per;
+    *splits = (n_kv + per - 1) / per;
+}
+
 // Validated launch on the current device (the caller switched devices).
 int launch_on_current(const Resolved &r, int dev) {
     const bool qkv_aligned = aligned(r.q, 16) && aligned(r.k, 16) && aligned(r.v, 16) && r.qs % 8 == 0 &&
@@ -201,16 +270,42 @@ int launch_on_current(const Resolved &r, int dev) {
     p.o_f16 = r.o_dtype == NCZ_DTYPE_F16;
     const size_t vec_elems = p.o_f16 ? 8 : 4;
     p.o_vec = aligned(r.o, 16) && r.os % vec_elems == 0 && r.orow % vec_elems == 0;
-    const unsigned grid = static_cast<unsigned>(static_cast<size_t>(p.num_groups) * r.bh);
-
-    switch (r.d) {
-        case 16: return use_tma ? launch_variant<16, true>(tq, tk, tv, p, grid, dev, r.stream)
-                                : launch_variant<16, false>(tq, tk, tv, p, grid, dev, r.stream);
-        case 32: return use_tma ? launch_variant<32, true>(tq, tk, tv, p, grid, dev, r.stream)
-                                : launch_variant<32, false>(tq, tk, tv, p, grid, dev, r.stream);
-        default: return use_tma ? launch_variant<64, true>(tq, tk, tv, p, grid, dev, r.stream)
-                                : launch_variant<64, false>(tq, tk, tv, p, grid, dev, r.stream);
+    choose_splits(r, dev, &p.num_splits, &p.kv_per_split);
+    p.part_o = nullptr;
+    p.part_ml = nullptr;
+    void *ws = nullptr;
+    if (p.num_splits > 1) {
+        const size_t rows = static_cast<size_t>(p.num_splits) * r.bh * r.seq;
+        cudaMemPool_t pool;
+        int st = device_pool(dev, &pool);
+        if (st != NCZ_SUCCESS) return st;
+        const cudaError_t e = cudaMallocFromPoolAsync(&ws, rows * (r.d + 2) * sizeof(float), pool, r.stream);
+        if (e != cudaSuccess) return map_cuda_error(e);
+        p.part_o = static_cast<float *>(ws);
+        p.part_ml = p.part_o + rows * r.d;
     }
+    const unsigned grid =
+        static_cast<unsigned>(static_cast<size_t>(p.num_groups) * r.bh * static_cast<size_t>(p.num_splits));
+    int st;
+    switch (r.d) {
+        case 16: st = use_tma ? launch_variant<16, true>(tq, tk, tv, p, grid, dev, r.stream)
+                              : launch_variant<16, false>(tq, tk, tv, p, grid, dev, r.stream);
+            if (st == NCZ_SUCCESS && p.num_splits > 1) st = launch_combine<16>(p, r.stream);
+            break;
+        case 32: st = use_tma ? launch_variant<32, true>(tq, tk, tv, p, grid, dev, r.stream)
+                              : launch_variant<32, false>(tq, tk, tv, p, grid, dev, r.stream);
+            if (st == NCZ_SUCCESS && p.num_splits > 1) st = launch_combine<32>(p, r.stream);
+            break;
+        default: st = use_tma ? launch_variant<64, true>(tq, tk, tv, p, grid, dev, r.stream)
+                              : launch_variant<64, false>(tq, tk, tv, p, grid, dev, r.stream);
+            if (st == NCZ_SUCCESS && p.num_splits > 1) st = launch_combine<64>(p, r.stream);
+            break;
+    }
+    if (ws != nullptr) {
+        const cudaError_t e = cudaFreeAsync(ws, r.stream);
+        if (st == NCZ_SUCCESS && e != cudaSuccess) st = map_cuda_error(e);
+    }
+    return st;
 }
 
 // Switches to r.device when given, launches, restores the caller's device.
@@ -424,6 +519,13 @@ int ncz_flash_launch(const void *q, size_t q_len, const void *k, size_t k_len, c
 int ncz_flash_fwd_ex(const ncz_flash_desc *desc) {
     if (desc == nullptr) return NCZ_ERROR_INVALID_VALUE;
     return launch_resolved(from_desc(*desc));
+}
+
+int ncz_flash_fwd_splits(const ncz_flash_desc *desc, int splits) {
+    if (desc == nullptr || splits < 0) return NCZ_ERROR_INVALID_VALUE;
+    Resolved r = from_desc(*desc);
+    r.splits = splits;
+    return launch_resolved(r);
 }
 
 int ncz_flash_fwd_multi(const ncz_flash_desc *descs, int count) {

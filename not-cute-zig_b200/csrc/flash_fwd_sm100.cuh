@@ -103,6 +103,14 @@ struct FlashParams {
     int causal;
     int o_f16;
     int o_vec;  // 16-byte vector stores of O are aligned
+    // Split-KV: num_splits > 1 splits each Q group's K tiles into ranges of
+    // kv_per_split tiles, one CTA per range; CTAs then write unnormalised partial
+    // O rows to part_o [split][slice][row][D] and (base m, sum l) pairs to
+    // part_ml [split][slice][row][2] for combine_splits.  1 = direct output.
+    int num_splits;
+    int kv_per_split;
+    float *part_o;
+    float *part_ml;
 };
 
 template <int D>
@@ -143,7 +151,10 @@ struct SmemLayout {
 struct Work {
     int slice;
     int q_base;
-    int n[kQTiles];  // K/V tiles each Q tile visits (0 = tile beyond seq_len)
+    int split;
+    int kv0;            // first K tile of this CTA's range
+    int n[kQTiles];     // K/V tiles each Q tile visits in the range (0 = none)
+    int diag[kQTiles];  // last K tile a Q tile sees at all (the only one with masked keys)
     int n_max;
 };
 
@@ -153,9 +164,13 @@ __device__ __forceinline__ Work make_work(const FlashParams &p) {
     Work wk;
     const int item = static_cast<int>(blockIdx.x);
     // Heaviest (last) Q-tile groups first: under causal masking they visit the most K tiles.
-    const int group = p.num_groups - 1 - item / p.batch_heads;
-    wk.slice = item % p.batch_heads;
+    const int per_group = p.batch_heads * p.num_splits;
+    const int group = p.num_groups - 1 - item / per_group;
+    const int rem = item % per_group;
+    wk.slice = rem / p.num_splits;
+    wk.split = rem % p.num_splits;
     wk.q_base = group * (kQTiles * kBlockM);
+    wk.kv0 = wk.split * p.kv_per_split;
     const int n_kv = (p.seq_len + kBlockN - 1) / kBlockN;
     wk.n_max = 0;
 #pragma unroll
@@ -163,7 +178,10 @@ __device__ __forceinline__ Work make_work(const FlashParams &p) {
         const int q0 = wk.q_base + w * kBlockM;
         const int last_row = min(q0 + kBlockM, p.seq_len) - 1;
         // causal (reference tile_end, src/flash_h64_bn32.zig:80-84): K tiles up to the diagonal
-        wk.n[w] = q0 >= p.seq_len ? 0 : (p.causal ? last_row / kBlockN + 1 : n_kv);
+        const int total = q0 >= p.seq_len ? 0 : (p.causal ? last_row / kBlockN + 1 : n_kv);
+        const int end = min(total, wk.kv0 + p.kv_per_split);
+        wk.n[w] = end > wk.kv0 ? end - wk.kv0 : 0;
+        wk.diag[w] = total - 1;
         wk.n_max = wk.n[w] > wk.n_max ? wk.n[w] : wk.n_max;
     }
     return wk;
@@ -196,6 +214,31 @@ __device__ __forceinline__ bool bounded_wait(uint32_t bar, uint32_t parity, vola
     return bounded_wait_slow(bar, parity, abort_flag, site, honor_abort);
 }
 
+// Same wait with the slow loop inlined: for waits taken while many registers
+// are live, where an out-of-line call would make the caller spill them.
+__device__ __forceinline__ bool warp_wait_inline(uint32_t bar, uint32_t parity, volatile uint32_t *abort_flag,
+                                                 uint32_t site) {
+    bool ok = mbar_try_wait(bar, parity);
+    if (!ok) {
+        const unsigned long long t0 = sm_clock();
+        for (uint32_t it = 1;; ++it) {
+            if (mbar_try_wait(bar, parity)) {
+                ok = true;
+                break;
+            }
+            if ((it & 15u) == 0u) {
+                if (*abort_flag) break;
+                if (sm_clock() - t0 > kWaitLimitCycles) {
+                    *abort_flag = 1u;
+                    atomicCAS(&g_ncz_status, 0u, 0x80000000u | (site << 24) | (blockIdx.x & 0xFFFFFFu));
+                    break;
+                }
+            }
+        }
+    }
+    return __all_sync(0xffffffffu, ok);
+}
+
 // All lanes wait; the result is made warp-uniform so .sync.aligned tcgen05
 // instructions that follow stay convergent.
 __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile uint32_t *abort_flag,
@@ -224,9 +267,12 @@ struct Bars {
 // ---------------------------------------------------------------------------
 // producer, TMA variant (whole warp; elect.sync picks the issuing lane)
 // ---------------------------------------------------------------------------
+// Loads that need no free-slot wait: Q and the first min(kStages, n_max) K/V
+// tiles.  Runs before the CTA-wide barrier that publishes the TMEM address, so
+// these copies overlap the TMEM allocation.  Returns the number of K/V tiles issued.
 template <int D>
-__device__ __forceinline__ void producer_tma(const CUtensorMap *tq, const CUtensorMap *tk, const CUtensorMap *tv,
-                                             uint32_t sbase, const Work &wk, volatile uint32_t *abort_flag) {
+__device__ __forceinline__ int producer_tma_prologue(const CUtensorMap *tq, const CUtensorMap *tk,
+                                                     const CUtensorMap *tv, uint32_t sbase, const Work &wk) {
     using L = SmemLayout<D>;
     const Bars<D> b{sbase};
     uint32_t qbytes = 0;
@@ -237,15 +283,31 @@ __device__ __forceinline__ void producer_tma(const CUtensorMap *tq, const CUtens
     for (int w = 0; w < kQTiles; ++w)
         if (wk.n[w] > 0)
             tma_load_3d_elect(sbase + L::kOffQ + w * L::kQTile, tq, b.q_full(), 0, wk.q_base + w * kBlockM, wk.slice);
-    int j = 0;
+    const int first = wk.n_max < L::kStages ? wk.n_max : L::kStages;
+    for (int j = 0; j < first; ++j) {
+        mbar_arrive_expect_tx_elect(b.k_full(j), L::kKvTile);
+        tma_load_3d_elect(sbase + L::kOffK + j * L::kKvTile, tk, b.k_full(j), 0, (wk.kv0 + j) * kBlockN, wk.slice);
+        mbar_arrive_expect_tx_elect(b.v_full(j), L::kKvTile);
+        tma_load_3d_elect(sbase + L::kOffV + j * L::kKvTile, tv, b.v_full(j), 0, (wk.kv0 + j) * kBlockN, wk.slice);
+    }
+    return first;
+}
+
+// The remaining K/V tiles (from j_begin), each after its ring slot is released.
+template <int D>
+__device__ __forceinline__ void producer_tma(const CUtensorMap *tk, const CUtensorMap *tv, uint32_t sbase,
+                                             const Work &wk, int j_begin, volatile uint32_t *abort_flag) {
+    using L = SmemLayout<D>;
+    const Bars<D> b{sbase};
+    int j = j_begin;
     for (; j < wk.n_max; ++j) {
         const int st = j % L::kStages;
         if (j >= L::kStages && !warp_wait(b.kv_empty(st), ((j / L::kStages) - 1) & 1, abort_flag, kSiteKvEmpty))
             break;
         mbar_arrive_expect_tx_elect(b.k_full(st), L::kKvTile);
-        tma_load_3d_elect(sbase + L::kOffK + st * L::kKvTile, tk, b.k_full(st), 0, j * kBlockN, wk.slice);
+        tma_load_3d_elect(sbase + L::kOffK + st * L::kKvTile, tk, b.k_full(st), 0, (wk.kv0 + j) * kBlockN, wk.slice);
         mbar_arrive_expect_tx_elect(b.v_full(st), L::kKvTile);
-        tma_load_3d_elect(sbase + L::kOffV + st * L::kKvTile, tv, b.v_full(st), 0, j * kBlockN, wk.slice);
+        tma_load_3d_elect(sbase + L::kOffV + st * L::kKvTile, tv, b.v_full(st), 0, (wk.kv0 + j) * kBlockN, wk.slice);
     }
     // Every issued copy must land before shared memory is released.
     bounded_wait(b.q_full(), 0, abort_flag, kSiteProducerDrain, false);
@@ -303,11 +365,11 @@ __device__ __forceinline__ void producer_lsu(const FlashParams &p, uint8_t *smem
         const int st = j % L::kStages;
         if (j >= L::kStages && !warp_wait(b.kv_empty(st), ((j / L::kStages) - 1) & 1, abort_flag, kSiteKvEmpty))
             break;
-        lsu_tile<D, kBlockN>(smem + L::kOffK + st * L::kKvTile, ks, p.k_row, j * kBlockN, p.seq_len, lane);
+        lsu_tile<D, kBlockN>(smem + L::kOffK + st * L::kKvTile, ks, p.k_row, (wk.kv0 + j) * kBlockN, p.seq_len, lane);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(b.k_full(st));
-        lsu_tile<D, kBlockN>(smem + L::kOffV + st * L::kKvTile, vs, p.v_row, j * kBlockN, p.seq_len, lane);
+        lsu_tile<D, kBlockN>(smem + L::kOffV + st * L::kKvTile, vs, p.v_row, (wk.kv0 + j) * kBlockN, p.seq_len, lane);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(b.v_full(st));
@@ -435,37 +497,50 @@ __device__ __forceinline__ void store_cols(uint32_t taddr, const float (&o)[N]) 
     }
 }
 
-// Writes O[row][0 .. N) = o / l (f32 or f16, vector stores when aligned).
+// Writes O[row][0 .. N) = o / l (f32 or f16, vector stores when aligned), as
+// o * (1 / l): one division per row instead of N.
 template <int N>
 __device__ __forceinline__ void write_o_global(const FlashParams &p, const Work &wk, int row, const float (&o)[N],
                                                float l) {
+    const float inv = 1.0f / l;
     if (p.o_f16) {
         __half *orow = reinterpret_cast<__half *>(p.o) + wk.slice * p.o_stride + static_cast<long long>(row) * p.o_row;
         if (p.o_vec) {
 #pragma unroll
             for (int c = 0; c < N; c += 8) {
                 uint4 v;
-                v.x = pack_f16x2(o[c + 0] / l, o[c + 1] / l);
-                v.y = pack_f16x2(o[c + 2] / l, o[c + 3] / l);
-                v.z = pack_f16x2(o[c + 4] / l, o[c + 5] / l);
-                v.w = pack_f16x2(o[c + 6] / l, o[c + 7] / l);
+                v.x = pack_f16x2(o[c + 0] * inv, o[c + 1] * inv);
+                v.y = pack_f16x2(o[c + 2] * inv, o[c + 3] * inv);
+                v.z = pack_f16x2(o[c + 4] * inv, o[c + 5] * inv);
+                v.w = pack_f16x2(o[c + 6] * inv, o[c + 7] * inv);
                 *reinterpret_cast<uint4 *>(orow + c) = v;
             }
         } else {
 #pragma unroll
-            for (int c = 0; c < N; ++c) orow[c] = __float2half_rn(o[c] / l);
+            for (int c = 0; c < N; ++c) orow[c] = __float2half_rn(o[c] * inv);
         }
     } else {
         float *orow = reinterpret_cast<float *>(p.o) + wk.slice * p.o_stride + static_cast<long long>(row) * p.o_row;
         if (p.o_vec) {
 #pragma unroll
             for (int c = 0; c < N; c += 4)
-                *reinterpret_cast<float4 *>(orow + c) = make_float4(o[c] / l, o[c + 1] / l, o[c + 2] / l, o[c + 3] / l);
+                *reinterpret_cast<float4 *>(orow + c) = make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv, o[c + 3] * inv);
         } else {
 #pragma unroll
-            for (int c = 0; c < N; ++c) orow[c] = o[c] / l;
+            for (int c = 0; c < N; ++c) orow[c] = o[c] * inv;
         }
     }
+}
+
+// Split-KV partial result of one row: O unnormalised (relative to base m) and (m, l).
+template <int D>
+__device__ __forceinline__ void write_partial(const FlashParams &p, const Work &wk, int row, const float (&o)[D],
+                                              float m, float l) {
+    const long long idx = (static_cast<long long>(wk.split) * p.batch_heads + wk.slice) * p.seq_len + row;
+    float *dst = p.part_o + idx * D;
+#pragma unroll
+    for (int c = 0; c < D; c += 4) *reinterpret_cast<float4 *>(dst + c) = make_float4(o[c], o[c + 1], o[c + 2], o[c + 3]);
+    *reinterpret_cast<float2 *>(p.part_ml + idx * 2) = make_float2(m, l);
 }
 
 // Row max of kBlockN scores with 8 independent chains: chain i covers x[i], x[8+i], ...
@@ -506,6 +581,55 @@ __device__ __forceinline__ float exp_row(float (&x)[kBlockN], float kmul, float 
     return s0 + s1;
 }
 
+// Keys of tile j a row may see: keys >= seq_len and, under causal masking,
+// keys > row are masked (reference: src/flash_h64_bn32.zig:122-135).
+__device__ __forceinline__ int lim_of(const FlashParams &p, int row, int j) {
+    int lim = p.seq_len - j * kBlockN;
+    if (p.causal) lim = min(lim, row - j * kBlockN + 1);
+    return lim;
+}
+
+// Scores of half H (keys 64H .. 64H+63) as the exponent's input: pre-scaled when
+// scale <= 0, masked keys at -inf.  Only the last K tile of a Q tile holds masked
+// keys: a Q tile's rows share one 128-key tile index.
+template <int H>
+__device__ __forceinline__ void prep_scores(float (&x)[kBlockN], bool pre_scale, float scale_log2, bool last,
+                                            int lim) {
+    constexpr int c0 = H * kBlockN / 2;
+    if (pre_scale) {
+#pragma unroll
+        for (int c = c0; c < c0 + kBlockN / 2; ++c) x[c] *= scale_log2;
+    }
+    if (last && lim < c0 + kBlockN / 2) {
+#pragma unroll
+        for (int c = c0; c < c0 + kBlockN / 2; ++c) x[c] = c < lim ? x[c] : -INFINITY;
+    }
+}
+
+// Exponentiates keys c0 .. c0+31 against base m (log2 domain), packs P to f16
+// pairs (rounded as src/flash_h64_bn32.zig:185) and sums the unrounded values.
+__device__ __forceinline__ float exp_chunk(const float (&x)[kBlockN], int c0, float kmul, float m,
+                                           uint32_t (&pk)[16]) {
+    const uint64_t kmul2 = pack_f32x2(kmul, kmul), negm2 = pack_f32x2(-m, -m);
+    uint64_t sum2[2] = {0ull, 0ull};  // (0.0f, 0.0f) x 2
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+        float e0, e1, p0, p1;
+        unpack_f32x2(ffma2(pack_f32x2(x[c0 + 2 * c], x[c0 + 2 * c + 1]), kmul2, negm2), e0, e1);
+        if (kExp2EmuPeriod > 0 && c % kExp2EmuPeriod >= kExp2EmuPeriod - kExp2EmuCount) {
+            exp2_poly_x2(e0, e1, p0, p1);  // FMA pipe
+        } else {
+            p0 = ex2_approx(e0);  // MUFU
+            p1 = ex2_approx(e1);
+        }
+        sum2[c & 1] = fadd2(sum2[c & 1], pack_f32x2(p0, p1));
+        pk[c] = pack_f16x2(p0, p1);
+    }
+    float s0, s1;
+    unpack_f32x2(fadd2(sum2[0], sum2[1]), s0, s1);
+    return s0 + s1;
+}
+
 template <int D>
 __device__ __forceinline__ void softmax_role(const FlashParams &p, uint32_t sbase, uint32_t tmem, const Work &wk,
                                              volatile uint32_t *abort_flag, int warp, int lane) {
@@ -541,27 +665,22 @@ __device__ __forceinline__ void softmax_role(const FlashParams &p, uint32_t sbas
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(b.s_free(w));  // S may be overwritten by the next QK^T
-
-        if (pre_scale) {
+        const int jg = wk.kv0 + j;  // K tile index in the sequence
+        prep_scores<0>(x, pre_scale, p.scale_log2, jg == wk.diag[w], lim_of(p, row, jg));
+        prep_scores<1>(x, pre_scale, p.scale_log2, jg == wk.diag[w], lim_of(p, row, jg));
+        float mx[8];
 #pragma unroll
-            for (int c = 0; c < kBlockN; ++c) x[c] *= p.scale_log2;
-        }
-        // masking (reference: src/flash_h64_bn32.zig:122-135): keys >= seq_len and,
-        // under causal masking, keys > row.  Only the last K tile of a Q tile holds
-        // either: a Q tile's rows share one 128-key tile index.
-        if (j == n - 1) {
-            int lim = seq_len - j * kBlockN;
-            if (p.causal) lim = min(lim, row - j * kBlockN + 1);
-            if (lim < kBlockN) {
+        for (int i = 0; i < 8; ++i) mx[i] = fmaxf(x[i], x[8 + i]);
 #pragma unroll
-                for (int c = 0; c < kBlockN; ++c) x[c] = c < lim ? x[c] : -INFINITY;
-            }
+        for (int c = 16; c < kBlockN; c += 16) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) mx[i] = fmax3(mx[i], x[c + i], x[c + 8 + i]);
         }
-        const float m_new = fmaxf(m, row_max(x) * kmul);
+        const float m_tile = fmaxf(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], fmax3(mx[5], mx[6], mx[7])));
+        const float m_new = fmaxf(m, m_tile * kmul);
         const bool need = m_new > m + kRescaleThreshold;
         float m_use = need ? m_new : m;
         m_use = m_use == -INFINITY ? 0.0f : m_use;  // row with nothing visible yet
-        const float alpha = ex2_approx(m - m_use);  // 1 when not rescaling, 0 on the first tile
 
         // The two softmax warps of a sub-partition (Q tiles 0 and 1) share its MUFU
         // unit; optionally they take turns: tile j of Q tile 0, tile j of Q tile 1, ...
@@ -575,9 +694,9 @@ __device__ __forceinline__ void softmax_role(const FlashParams &p, uint32_t sbas
             __syncwarp();
             if (lane == 0) mbar_arrive(b.turn(sub, w ^ 1));
         }
+        const float alpha = ex2_approx(m - m_use);  // 1 when not rebasing, 0 on the first tile
         l = l * alpha + tsum;
         m = m_use;
-
         if (j > 0) {
             // PV(j-1) reads P and accumulates into O: it must be done before P is
             // overwritten and before O is rebased.
@@ -605,7 +724,13 @@ __device__ __forceinline__ void softmax_role(const FlashParams &p, uint32_t sbas
             tc_fence_after();
             float o[D];
             load_cols<D>(tO, o);
-            if (row < seq_len) write_o_global<D>(p, wk, row, o, l);
+            if (row < seq_len) {
+                if (p.num_splits > 1) {
+                    write_partial<D>(p, wk, row, o, m, l);
+                } else {
+                    write_o_global<D>(p, wk, row, o, l);
+                }
+            }
         }
     }
 }
@@ -645,10 +770,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         *abort_flag = 0u;
         mbar_fence_init();
     }
-    if (kTma && warp == 0 && lane == 0) {
-        tma_prefetch_map(&tmap_q);
-        tma_prefetch_map(&tmap_k);
-        tma_prefetch_map(&tmap_v);
+    int issued = 0;
+    if (kTma && warp == 0) {
+        __syncwarp();  // barrier initialisation (thread 0) is visible to the warp
+        if (lane == 0) {
+            tma_prefetch_map(&tmap_q);
+            tma_prefetch_map(&tmap_k);
+            tma_prefetch_map(&tmap_v);
+        }
+        issued = producer_tma_prologue<D>(&tmap_q, &tmap_k, &tmap_v, sbase, wk);
     }
     if (warp == 1) {
         tmem_alloc(sbase + L::kOffTmemSlot, kTmemCols);
@@ -661,7 +791,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == 0) {
         if constexpr (kTma) {
-            producer_tma<D>(&tmap_q, &tmap_k, &tmap_v, sbase, wk, abort_flag);
+            producer_tma<D>(&tmap_k, &tmap_v, sbase, wk, issued, abort_flag);
         } else {
             producer_lsu<D>(p, smem, sbase, wk, abort_flag, lane);
         }
@@ -677,6 +807,66 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// split-KV combine: one warp per (slice, row), D/32 .. 2 columns per lane
+// ---------------------------------------------------------------------------
+constexpr int kMaxSplits = 8;
+
+// O = sum_i 2^(m_i - M) O_i / sum_i 2^(m_i - M) l_i over the splits whose K
+// range the row reaches, M = max_i m_i (the flash-decoding reduction of the
+// per-split online-softmax states).  All splits' loads are issued together.
+template <int D>
+__global__ void __launch_bounds__(256) combine_splits(const __grid_constant__ FlashParams p) {
+    constexpr int kPer = D >= 32 ? D / 32 : 1;  // columns per lane
+    constexpr int kLanes = D / kPer;
+    const int lane = static_cast<int>(threadIdx.x & 31);
+    const long long rid = static_cast<long long>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+    if (rid >= static_cast<long long>(p.batch_heads) * p.seq_len) return;
+    const int slice = static_cast<int>(rid / p.seq_len), row = static_cast<int>(rid % p.seq_len);
+    const int n_kv = (p.seq_len + kBlockN - 1) / kBlockN;
+    const int total = p.causal ? row / kBlockN + 1 : n_kv;  // K tiles of this row's Q tile
+    const int splits = min(p.num_splits, (total + p.kv_per_split - 1) / p.kv_per_split);
+    const long long stride = static_cast<long long>(p.batch_heads) * p.seq_len;  // rows per split
+    const long long idx0 = static_cast<long long>(slice) * p.seq_len + row;
+    float2 ml[kMaxSplits];
+    float part[kMaxSplits][kPer];
+#pragma unroll
+    for (int i = 0; i < kMaxSplits; ++i) {
+        const bool on = i < splits;
+        ml[i] = on ? __ldg(reinterpret_cast<const float2 *>(p.part_ml) + idx0 + i * stride) : make_float2(-INFINITY, 0.0f);
+#pragma unroll
+        for (int c = 0; c < kPer; ++c)
+            part[i][c] = on && lane < kLanes ? __ldg(p.part_o + (idx0 + i * stride) * D + lane * kPer + c) : 0.0f;
+    }
+    float mmax = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < kMaxSplits; ++i) mmax = fmaxf(mmax, ml[i].x);
+    float acc[kPer];
+#pragma unroll
+    for (int c = 0; c < kPer; ++c) acc[c] = 0.0f;
+    float lsum = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kMaxSplits; ++i) {
+        if (i < splits) {
+            const float wgt = ex2_approx(ml[i].x - mmax);
+            lsum += wgt * ml[i].y;
+#pragma unroll
+            for (int c = 0; c < kPer; ++c) acc[c] += wgt * part[i][c];
+        }
+    }
+    if (lane >= kLanes) return;
+    const float inv = 1.0f / lsum;
+    const long long base = slice * p.o_stride + static_cast<long long>(row) * p.o_row + lane * kPer;
+#pragma unroll
+    for (int c = 0; c < kPer; ++c) {
+        if (p.o_f16) {
+            reinterpret_cast<__half *>(p.o)[base + c] = __float2half_rn(acc[c] * inv);
+        } else {
+            reinterpret_cast<float *>(p.o)[base + c] = acc[c] * inv;
+        }
     }
 }
 

@@ -108,6 +108,7 @@ _SIGNATURES = {
     "ncz_flash_fwd_ex": (ctypes.c_int, [ctypes.POINTER(_Desc)]),
     "ncz_flash_fwd_multi": (ctypes.c_int, [ctypes.POINTER(_Desc), ctypes.c_int]),
     "ncz_flash_fwd_host": (ctypes.c_int, [ctypes.POINTER(_Desc), _VP, _VP, _VP, _VP, _SZ]),
+    "ncz_flash_fwd_splits": (ctypes.c_int, [ctypes.POINTER(_Desc), ctypes.c_int]),
     "ncz_flash_sync_status": (ctypes.c_int, [ctypes.c_int, _VP, ctypes.POINTER(ctypes.c_uint32)]),
     "ncz_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "ncz_launch_count": (ctypes.c_uint64, []),
@@ -267,6 +268,14 @@ def launch_ex(q, k, v, o, opts: Options, *, row_strides: Optional[Sequence[int]]
     """ncz_flash_fwd_ex: the reference launch plus the layout extensions."""
     d = make_desc(q, k, v, o, opts, row_strides=row_strides, producer=producer, device=device, stream=stream)
     _check(lib().ncz_flash_fwd_ex(ctypes.byref(d)), "flash.launch_ex")
+
+
+def launch_splits(q, k, v, o, opts: Options, splits: int, *, row_strides: Optional[Sequence[int]] = None,
+                  producer: str = "auto", stream=None) -> None:
+    """ncz_flash_fwd_splits: launch_ex with an explicit split-KV request
+    (0 = automatic, 1 = no split, n = up to n K ranges merged by a second kernel)."""
+    d = make_desc(q, k, v, o, opts, row_strides=row_strides, producer=producer, stream=stream)
+    _check(lib().ncz_flash_fwd_splits(ctypes.byref(d), int(splits)), "flash.launch_splits")
 
 
 def launch_host(q_host, k_host, v_host, o_host, q, k, v, o, opts: Options, *, chunk_slices: int = 0,

@@ -20,7 +20,7 @@ if not torch.cuda.is_available():
 SENTINEL = 12345.0
 
 
-def run(ncz, p: C.Problem, *, o_dtype="float32", producer="auto", via="auto"):
+def run(ncz, p: C.Problem, *, o_dtype="float32", producer="auto", via="auto", splits=None):
     dev = torch.device("cuda:0")
     q = torch.from_numpy(p.q).to(dev)
     k = torch.from_numpy(p.k).to(dev)
@@ -30,7 +30,9 @@ def run(ncz, p: C.Problem, *, o_dtype="float32", producer="auto", via="auto"):
                        v_stride=p.strides[2], o_stride=p.strides[3], scale=p.scale, batch_heads=p.bh,
                        causal=p.causal)
     plain = p.row_strides is None and o_dtype == "float32" and producer == "auto"
-    if via == "launch" or (via == "auto" and plain):
+    if splits is not None:
+        ncz.launch_splits(q, k, v, o, opts, splits, row_strides=p.row_strides, producer=producer)
+    elif via == "launch" or (via == "auto" and plain):
         ncz.launch(q, k, v, o, opts)
     else:
         ncz.launch_ex(q, k, v, o, opts, row_strides=p.row_strides, producer=producer)
@@ -252,3 +254,79 @@ def test_host_pipeline_matches_device_launch(ncz, oracle_mod, chunk, o_dtype):
     ti = torch.from_numpy(idx)
     assert torch.equal(got[ti], want[ti])
     C.check(got.float().numpy(), C.reference(p, oracle_mod), idx, f"host pipeline chunk={chunk} {o_dtype}")
+
+
+SPLIT_CASES = [(4, 1024, 64, True), (3, 1000, 64, False), (2, 777, 32, True), (5, 1300, 16, True),
+               (1, 4096, 64, True)]
+
+
+@pytest.mark.parametrize("case", SPLIT_CASES, ids=lambda c: f"bh{c[0]}_s{c[1]}_d{c[2]}_c{int(c[3])}")
+@pytest.mark.parametrize("splits", [2, 3, 8])
+def test_split_kv_matches_oracle(ncz, oracle_mod, case, splits):
+    """Split-KV (K ranges on separate CTAs, merged by combine_splits) against the
+    oracle, next to the unsplit launch; nothing outside the active rows is written."""
+    bh, s, d, causal = case
+    p = C.normal_problem(bh, s, d, causal, 71, oracle_mod, std=0.8)
+    want = C.reference(p, oracle_mod)
+    idx = C.active_index(p)
+    for sp in (1, splits):
+        got = run(ncz, p, splits=sp)
+        C.check(got, want, idx, f"split-KV splits={sp} {case}")
+        assert untouched(got, p, idx)
+
+
+def test_config2_split_and_unsplit_match(ncz, oracle_mod):
+    """BASELINE config 2 (bh=8, S=1024, d=64, causal, f16 O): the automatic
+    choice does not split (8 K tiles are too few to pay for a second launch);
+    a forced 4-way split gives the same result within tolerance."""
+    p = C.normal_problem(8, 1024, 64, True, 1, oracle_mod, std=0.5)
+    want = C.reference(p, oracle_mod)
+    idx = C.active_index(p)
+    before = ncz.flash.launch_count()
+    auto = run(ncz, p, o_dtype="float16", splits=0)
+    assert ncz.flash.launch_count() - before == 1
+    C.check(auto, want, idx, "config 2 auto (f16 O)")
+    before = ncz.flash.launch_count()
+    split = run(ncz, p, o_dtype="float16", splits=4)
+    assert ncz.flash.launch_count() - before == 2  # forward + combine
+    C.check(split, want, idx, "config 2 split 4 (f16 O)")
+
+
+def test_long_sequence_few_slices_splits_automatically(ncz, oracle_mod):
+    """bh=1, S=4096 causal: 16 CTAs for 32 K tiles, so the automatic choice splits
+    (forward + combine) and matches the oracle."""
+    p = C.normal_problem(1, 4096, 64, True, 5, oracle_mod, std=0.7)
+    before = ncz.flash.launch_count()
+    got = run(ncz, p, splits=0)
+    assert ncz.flash.launch_count() - before == 2
+    C.check(got, C.reference(p, oracle_mod), C.active_index(p), "bh=1 S=4096 auto split")
+
+
+@pytest.mark.parametrize("d", [16, 32, 64])
+def test_split_kv_tma_equals_lsu(ncz, oracle_mod, d):
+    """Both producers give bit-identical split results (same partials, same merge)."""
+    p = C.normal_problem(3, 900, d, True, 81, oracle_mod, std=0.6)
+    a = run(ncz, p, splits=4, producer="tma")
+    b = run(ncz, p, splits=4, producer="lsu")
+    assert np.array_equal(a, b)
+    assert np.array_equal(run(ncz, p, splits=4, producer="tma"), a)
+
+
+def test_split_kv_repeated_launches_and_streams(ncz, oracle_mod):
+    """Repeated split launches (partials in the stream-ordered pool) on one stream
+    and on a second stream stay bit-identical."""
+    p = C.normal_problem(4, 2048, 64, True, 91, oracle_mod, std=0.7)
+    first = run(ncz, p, splits=4)
+    for _ in range(3):
+        assert np.array_equal(run(ncz, p, splits=4), first)
+    dev = torch.device("cuda:0")
+    q, k, v = (torch.from_numpy(a).to(dev) for a in (p.q, p.k, p.v))
+    opts = ncz.Options(seq_len=p.seq, head_dim=p.d, q_stride=p.strides[0], k_stride=p.strides[1],
+                       v_stride=p.strides[2], o_stride=p.strides[3], scale=p.scale, batch_heads=p.bh, causal=True)
+    side = torch.cuda.Stream(dev)
+    for _ in range(2):
+        o = torch.full((p.bh * p.strides[3],), SENTINEL, dtype=torch.float32, device=dev)
+        ncz.launch_splits(q, k, v, o, opts, 4, stream=side)
+        side.synchronize()
+        assert np.array_equal(o.cpu().numpy(), first)
+    assert ncz.sync_status() == 0
