@@ -42,12 +42,13 @@ NOMINAL_F16_TFLOPS = 2250.0
 FALLBACK_TFLOPS = 1590.0
 
 WORKLOADS = {
-    # name: (batch_heads per GPU, seq_len, head_dim, causal, std, k_mul, seed, description)
-    "c4": (64, 8192, 64, True, 1.0, 2.0, 3, "config4_long_causal bh=64 S=8192 d=64 causal N(0,1) Kx2"),
-    "c2": (8, 1024, 64, True, 0.5, 1.0, 1, "config2_profile bh=8 S=1024 d=64 causal N(0,.25)"),
-    "c5": (1024, 2048, 64, False, 0.5, 1.0, 4, "config5_sweep bh=1024 S=2048 d=64 non-causal N(0,.25)"),
-    "c5d16": (1024, 2048, 16, False, 0.5, 1.0, 5, "config5_sweep bh=1024 S=2048 d=16 non-causal N(0,.25)"),
+    # name: (batch_heads per GPU, seq_len, head_dim, causal, std, k_mul, seed, O dtype, description)
+    "c4": (64, 8192, 64, True, 1.0, 2.0, 3, "f32", "config4_long_causal bh=64 S=8192 d=64 causal N(0,1) Kx2"),
+    "c2": (8, 1024, 64, True, 0.5, 1.0, 1, "f16", "config2_profile bh=8 S=1024 d=64 causal N(0,.25) f16 O"),
+    "c5": (1024, 2048, 64, False, 0.5, 1.0, 4, "f32", "config5_sweep bh=1024 S=2048 d=64 non-causal N(0,.25)"),
+    "c5d16": (1024, 2048, 16, False, 0.5, 1.0, 5, "f32", "config5_sweep bh=1024 S=2048 d=16 non-causal N(0,.25)"),
 }
+L2_BYTES = 126 * 1024 * 1024
 
 
 def flops_of(bh, s, d, causal):
@@ -133,16 +134,17 @@ def make_inputs(oracle, bh, s, d, std, k_mul, seed):
 # ---------------------------------------------------------------------------
 # CPU leg: the oracle (restated reference CPU attention) on a bounded sample
 # ---------------------------------------------------------------------------
-def cpu_sample(oracle, q, k, v, s, d, causal, scale, target_s, threads=0):
-    """Times the oracle on the last rows of slice 0 (the heaviest rows under
-    causal masking), sized to about target_s seconds.  Returns
-    (TFLOP/s, seconds, rows, flops, threads)."""
+def cpu_sample(oracle, q, k, v, s, d, causal, scale, target_s, threads=0, bh=1):
+    """Times the oracle on a bounded sample of the workload sized to about
+    target_s seconds: the last rows of slice 0 (the heaviest rows under causal
+    masking) when one slice is enough, else whole slices 0..m-1.  Returns
+    (TFLOP/s, seconds, description, flops, threads)."""
     import numpy as np
 
     threads = threads or oracle.max_threads()
-    out = np.zeros(s * d, dtype=np.float32)
 
-    def run(rows):
+    def run_rows(rows):
+        out = np.zeros(s * d, dtype=np.float32)
         r0 = s - rows
         t0 = time.perf_counter()
         oracle.flash_reference(q[: s * d], k[: s * d], v[: s * d], batch_heads=1, seq_len=s, head_dim=d,
@@ -152,14 +154,30 @@ def cpu_sample(oracle, q, k, v, s, d, causal, scale, target_s, threads=0):
         keys = sum((r + 1) if causal else s for r in range(r0, s))
         return dt, 4 * keys * d
 
+    def run_slices(m):
+        out = np.zeros(m * s * d, dtype=np.float32)
+        t0 = time.perf_counter()
+        oracle.flash_reference(q[: m * s * d], k[: m * s * d], v[: m * s * d], batch_heads=m, seq_len=s,
+                               head_dim=d, q_stride=s * d, k_stride=s * d, v_stride=s * d, o_stride=s * d,
+                               scale=scale, causal=causal, out=out, threads=threads)
+        dt = time.perf_counter() - t0
+        keys = (s * (s + 1) // 2) if causal else s * s
+        return dt, 4 * m * keys * d
+
     rows = min(s, max(threads, 8))
-    dt, fl = run(rows)
+    dt, fl = run_rows(rows)
     while dt < 0.5 and rows < s:
         rows = min(s, rows * 4)
-        dt, fl = run(rows)
-    rows = min(s, max(threads, int(rows * target_s / max(dt, 1e-6))))
-    dt, fl = run(rows)
-    return fl / dt / 1e12, dt, rows, fl, threads
+        dt, fl = run_rows(rows)
+    if rows < s:
+        rows = min(s, max(threads, int(rows * target_s / max(dt, 1e-6))))
+    if rows < s:
+        dt, fl = run_rows(rows)
+        return fl / dt / 1e12, dt, f"rows {s - rows}..{s - 1} of slice 0", fl, threads, rows
+    dt1, _ = run_slices(1)
+    m = max(1, min(bh, int(target_s / max(dt1, 1e-6))))
+    dt, fl = run_slices(m)
+    return fl / dt / 1e12, dt, f"slices 0..{m - 1} (all rows)", fl, threads, s
 
 
 def cpu_model():
@@ -180,12 +198,12 @@ def reference_arm(args):
         return 0
     import oracle
 
-    bh, s, d, causal, std, k_mul, seed, desc = WORKLOADS[args.workload]
+    bh, s, d, causal, std, k_mul, seed, o_dtype, desc = WORKLOADS[args.workload]
     q, k, v = make_inputs(oracle, 1, s, d, std, k_mul, seed)
     scale = 1.0 / math.sqrt(d)
     threads = oracle.max_threads()
     budget = 90.0  # seconds of CPU work for the whole --steps/--warmup run
-    _, dt_cal, rows_cal, _, _ = cpu_sample(oracle, q, k, v, s, d, causal, scale, 1.0, threads)
+    _, dt_cal, _, _, _, rows_cal = cpu_sample(oracle, q, k, v, s, d, causal, scale, 1.0, threads)
     per_row = dt_cal / rows_cal
     rows = max(threads, int(budget / (args.steps + args.warmup) / per_row))
     rows = min(rows, s)
@@ -262,7 +280,7 @@ def main():
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
 
-    bh, s, d, causal, std, k_mul, seed, desc = WORKLOADS[args.workload]
+    bh, s, d, causal, std, k_mul, seed, o_dtype, desc = WORKLOADS[args.workload]
     scale = 1.0 / math.sqrt(d)
     n = bh * s * d
     # Weak scaling: every rank owns its own bh slices (seeded by rank).
@@ -270,7 +288,12 @@ def main():
     q = torch.from_numpy(hq).to(dev)
     k = torch.from_numpy(hk).to(dev)
     v = torch.from_numpy(hv).to(dev)
-    o = torch.empty(n, dtype=torch.float32, device=dev)
+    tdt = torch.float16 if o_dtype == "f16" else torch.float32
+    o = torch.empty(n, dtype=tdt, device=dev)
+    working_set = 3 * n * 2 + n * o.element_size()
+    # Inputs + O smaller than L2: flush L2 before every timed step (memset of a
+    # 256 MB buffer, outside the timed intervals).
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev) if working_set <= L2_BYTES else None
     opts = ncz.Options(seq_len=s, head_dim=d, q_stride=s * d, k_stride=s * d, v_stride=s * d, o_stride=s * d,
                        scale=scale, batch_heads=bh, causal=causal)
     stream = torch.cuda.current_stream(dev)
@@ -281,24 +304,40 @@ def main():
             dist.barrier()
         torch.cuda.synchronize(dev)
 
+    def step():
+        if o_dtype == "f16":
+            ncz.launch_ex(q, k, v, o, opts, stream=stream)
+        else:
+            ncz.launch(q, k, v, o, opts, stream=stream)
+
     for _ in range(args.warmup):
-        ncz.launch(q, k, v, o, opts, stream=stream)
+        step()
     ncz.sync_status(device=local, stream=stream)
     barrier()
     sampler = ClockSampler(local)
     time.sleep(0.3)  # let the sampler start
     barrier()
     launches0 = ncz.flash.launch_count()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record(stream)
-    for _ in range(args.steps):
-        ncz.launch(q, k, v, o, opts, stream=stream)
-    end.record(stream)
-    barrier()
+    if flush is None:
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        end.record(stream)
+        barrier()
+        ms = start.elapsed_time(end)
+    else:
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for e0, e1 in evs:
+            flush.zero_()
+            e0.record(stream)
+            step()
+            e1.record(stream)
+        barrier()
+        ms = sum(e0.elapsed_time(e1) for e0, e1 in evs)
     clocks = sampler.stop()
     launches = ncz.flash.launch_count() - launches0
     ncz.sync_status(device=local, stream=stream)
-    ms = start.elapsed_time(end)
     t = torch.tensor([ms], dtype=torch.float64, device=dev)
     if dist is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -313,7 +352,7 @@ def main():
     e2e = None
     if not args.no_e2e:
         pq, pk_, pv = (torch.from_numpy(a).pin_memory() for a in (hq, hk, hv))
-        po = torch.empty(n, dtype=torch.float32).pin_memory()
+        po = torch.empty(n, dtype=tdt).pin_memory()
         dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
 
         def e2e_step():
@@ -332,14 +371,14 @@ def main():
         if dist is not None:
             dist.all_reduce(et, op=dist.ReduceOp.MAX)
         e2e = {"value": world * step_flops * args.e2e_steps / (float(et.item()) / 1e3) / 1e12, "unit": "TFLOP/s",
-               "h2d_bytes_per_step": 3 * n * 2, "d2h_bytes_per_step": n * 4, "steps": args.e2e_steps,
+               "h2d_bytes_per_step": 3 * n * 2, "d2h_bytes_per_step": n * o.element_size(), "steps": args.e2e_steps,
                "api": "flash.launch_host -> ncz_flash_fwd_host (C ABI), default chunking"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        tf, dt, rows, fl, thr = cpu_sample(oracle, hq, hk, hv, s, d, causal, scale, args.cpu_seconds)
+        tf, dt, what, fl, thr, _ = cpu_sample(oracle, hq, hk, hv, s, d, causal, scale, args.cpu_seconds, bh=bh)
         cpu = {"value": tf, "unit": "TFLOP/s", "cores": thr, "kind": "port",
-               "sample": f"oracle (restatement of src/main.zig:1271-1307) on rows {s - rows}..{s - 1} of slice 0 "
+               "sample": f"oracle (restatement of src/main.zig:1271-1307) on {what} "
                          f"({fl / 1e9:.2f} GFLOP in {dt:.1f} s), {cpu_model()}"}
 
     if dist is not None:
@@ -354,9 +393,11 @@ def main():
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f16", "data": "synthetic",
             "config": {"workload": desc, "batch_heads_per_gpu": bh, "batch_heads_total": bh * world,
-                       "seq_len": s, "head_dim": d, "causal": causal, "o_dtype": "f32",
+                       "seq_len": s, "head_dim": d, "causal": causal, "o_dtype": o_dtype,
                        "parallelism": f"slices sharded x{world}, no collective",
-                       "l2": "inputs 3x%.0f MB + O %.0f MB > 126 MB L2; no flush" % (n * 2 / 1e6, n * 4 / 1e6)},
+                       "l2": ("inputs 3x%.1f MB + O %.1f MB > 126 MB L2; no flush" if flush is None else
+                              "inputs 3x%.1f MB + O %.1f MB fit in L2: 256 MB memset before every timed step, "
+                              "outside the timed intervals") % (n * 2 / 1e6, n * o.element_size() / 1e6)},
             "pct_peak_nominal": per_gpu / NOMINAL_F16_TFLOPS,
             "pct_peak_measured": per_gpu / peak,
             "roofline": {"bound": "tensor", "achieved": per_gpu, "peak": peak, "unit": "TFLOP/s",

@@ -137,6 +137,15 @@ int ncz_flash_fwd_ex(const ncz_flash_desc *desc);
  * (ceil(S/16), bh), src/flash.zig:45-69). */
 int ncz_flash_fwd_splits(const ncz_flash_desc *desc, int splits);
 
+/* ncz_flash_fwd_splits without any allocation: split-KV partials go to a
+ * static 16 MiB scratch array of the library's device image (one per device)
+ * instead of the memory pool.  The split count is lowered until the partials
+ * (splits x batch_heads x seq_len x (head_dim + 2) floats) fit, down to no
+ * split.  The array is shared by all such launches on a device, so they must
+ * be ordered (one stream, or event-ordered streams); ncz_flash_fwd_splits has
+ * no such restriction. */
+int ncz_flash_fwd_static(const ncz_flash_desc *desc, int splits);
+
 /* One call, several devices: descs[i] is launched on descs[i].device (each on
  * its own stream); the caller's current device is restored.  Used to shard
  * batch x head slices across GPUs.  The reference has one device only
@@ -146,7 +155,8 @@ int ncz_flash_fwd_multi(const ncz_flash_desc *descs, int count);
 /* Host-buffer forward with overlapped copies.  q_host, k_host, v_host and
  * o_host are HOST buffers laid out exactly like desc->q/k/v/o (same strides);
  * desc->q/k/v/o are caller-owned device buffers of the same layout that stage
- * them.  Slices are processed in chunks of chunk_slices (0 = bh/8 rounded up):
+ * them.  Slices are processed in chunks of chunk_slices (0 = bh/8 rounded up,
+ * but at least 4 MiB of Q/K/V per chunk):
  * a chunk's Q/K/V upload, its forward and its O download run on separate
  * streams, so the upload of chunk i+1 overlaps the forward of chunk i and the
  * download of chunk i-1.  Host buffers must be page-locked (pinned) for the

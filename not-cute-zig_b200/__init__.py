@@ -12,6 +12,7 @@ from .flash import (  # noqa: F401
     launch_host,
     launch_multi,
     launch_splits,
+    launch_static,
     select_kernel,
     sync_status,
 )

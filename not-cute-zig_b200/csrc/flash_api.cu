@@ -76,6 +76,9 @@ struct Resolved {
     int device;
     cudaStream_t stream;
     int splits = 0;  // split-KV request: 0 = automatic, 1 = none, n = n ranges
+    bool use_static = false;   // split-KV partials in the static scratch array, not the pool
+    float *scratch = nullptr;  // (resolved on the launch device)
+    size_t scratch_floats = 0;
 };
 
 bool mul_ok(size_t a, size_t b, size_t *out) { return !__builtin_mul_overflow(a, b, out); }
@@ -169,6 +172,24 @@ int launch_combine(const FlashParams &p, cudaStream_t stream) {
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return map_cuda_error(e);
     g_launches.fetch_add(1, std::memory_order_relaxed);
+    return NCZ_SUCCESS;
+}
+
+// Static split-KV scratch for ncz_flash_fwd_static: part of the module image,
+// so that entry point allocates nothing.  4 Mi floats = 16 MiB per device.
+constexpr size_t kStaticScratchFloats = size_t(4) << 20;
+__device__ float g_ncz_scratch[kStaticScratchFloats];
+float *g_scratch_addr[kMaxDevices];
+
+int static_scratch(int dev, float **out) {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (g_scratch_addr[dev] == nullptr) {
+        void *addr = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&addr, g_ncz_scratch);
+        if (e != cudaSuccess) return map_cuda_error(e);
+        g_scratch_addr[dev] = static_cast<float *>(addr);
+    }
+    *out = g_scratch_addr[dev];
     return NCZ_SUCCESS;
 }
 
@@ -271,10 +292,25 @@ int launch_on_current(const Resolved &r, int dev) {
     const size_t vec_elems = p.o_f16 ? 8 : 4;
     p.o_vec = aligned(r.o, 16) && r.os % vec_elems == 0 && r.orow % vec_elems == 0;
     choose_splits(r, dev, &p.num_splits, &p.kv_per_split);
+    if (r.scratch != nullptr) {
+        // Fixed scratch: the largest split count (<= the choice) whose partials fit.
+        const size_t per_split = r.bh * r.seq * (r.d + 2);
+        const int n_kv = static_cast<int>((r.seq + ncz::kBlockN - 1) / ncz::kBlockN);
+        int fit = static_cast<int>(std::min<size_t>(r.scratch_floats / per_split, size_t(ncz::kMaxSplits)));
+        if (fit < p.num_splits) {
+            const int want = std::max(1, fit);
+            p.kv_per_split = (n_kv + want - 1) / want;
+            p.num_splits = (n_kv + p.kv_per_split - 1) / p.kv_per_split;
+        }
+    }
     p.part_o = nullptr;
     p.part_ml = nullptr;
     void *ws = nullptr;
-    if (p.num_splits > 1) {
+    if (p.num_splits > 1 && r.scratch != nullptr) {
+        const size_t rows = static_cast<size_t>(p.num_splits) * r.bh * r.seq;
+        p.part_o = r.scratch;
+        p.part_ml = p.part_o + rows * r.d;
+    } else if (p.num_splits > 1) {
         const size_t rows = static_cast<size_t>(p.num_splits) * r.bh * r.seq;
         cudaMemPool_t pool;
         int st = device_pool(dev, &pool);
@@ -322,7 +358,14 @@ int launch_resolved(const Resolved &r) {
         e = cudaSetDevice(dev);
         if (e != cudaSuccess) return map_cuda_error(e);
     }
-    st = launch_on_current(r, dev);
+    if (r.use_static) {
+        Resolved rs = r;
+        st = static_scratch(dev, &rs.scratch);
+        rs.scratch_floats = kStaticScratchFloats;
+        if (st == NCZ_SUCCESS) st = launch_on_current(rs, dev);
+    } else {
+        st = launch_on_current(r, dev);
+    }
     if (dev != prev) cudaSetDevice(prev);
     return st;
 }
@@ -528,6 +571,14 @@ int ncz_flash_fwd_splits(const ncz_flash_desc *desc, int splits) {
     return launch_resolved(r);
 }
 
+int ncz_flash_fwd_static(const ncz_flash_desc *desc, int splits) {
+    if (desc == nullptr || splits < 0) return NCZ_ERROR_INVALID_VALUE;
+    Resolved r = from_desc(*desc);
+    r.splits = splits;
+    r.use_static = true;
+    return launch_resolved(r);
+}
+
 int ncz_flash_fwd_multi(const ncz_flash_desc *descs, int count) {
     if (descs == nullptr || count <= 0) return NCZ_ERROR_INVALID_VALUE;
     for (int i = 0; i < count; ++i) {
@@ -559,8 +610,14 @@ int ncz_flash_fwd_host(const ncz_flash_desc *desc, const void *q_host, const voi
         e = cudaSetDevice(dev);
         if (e != cudaSuccess) return map_cuda_error(e);
     }
-    // Default: 8 chunks, so one chunk's upload hides the previous chunk's forward.
-    const size_t chunk = chunk_slices > 0 ? chunk_slices : (r.bh + 7) / 8;
+    // Default: 8 chunks, so one chunk's upload hides the previous chunk's forward,
+    // but at least 4 MiB of Q/K/V per chunk (smaller copies cost more than they hide).
+    size_t chunk = chunk_slices;
+    if (chunk == 0) {
+        const size_t slice_bytes = (r.qs + r.ks + r.vs) * 2;
+        const size_t min_slices = ((size_t(4) << 20) + slice_bytes - 1) / slice_bytes;
+        chunk = std::max((r.bh + 7) / 8, min_slices);
+    }
     st = host_pipeline(r, q_host, k_host, v_host, o_host, chunk, dev);
     if (dev != prev) cudaSetDevice(prev);
     return st;

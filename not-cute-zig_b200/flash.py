@@ -109,6 +109,7 @@ _SIGNATURES = {
     "ncz_flash_fwd_multi": (ctypes.c_int, [ctypes.POINTER(_Desc), ctypes.c_int]),
     "ncz_flash_fwd_host": (ctypes.c_int, [ctypes.POINTER(_Desc), _VP, _VP, _VP, _VP, _SZ]),
     "ncz_flash_fwd_splits": (ctypes.c_int, [ctypes.POINTER(_Desc), ctypes.c_int]),
+    "ncz_flash_fwd_static": (ctypes.c_int, [ctypes.POINTER(_Desc), ctypes.c_int]),
     "ncz_flash_sync_status": (ctypes.c_int, [ctypes.c_int, _VP, ctypes.POINTER(ctypes.c_uint32)]),
     "ncz_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "ncz_launch_count": (ctypes.c_uint64, []),
@@ -276,6 +277,14 @@ def launch_splits(q, k, v, o, opts: Options, splits: int, *, row_strides: Option
     (0 = automatic, 1 = no split, n = up to n K ranges merged by a second kernel)."""
     d = make_desc(q, k, v, o, opts, row_strides=row_strides, producer=producer, stream=stream)
     _check(lib().ncz_flash_fwd_splits(ctypes.byref(d), int(splits)), "flash.launch_splits")
+
+
+def launch_static(q, k, v, o, opts: Options, splits: int = 0, *, row_strides: Optional[Sequence[int]] = None,
+                  producer: str = "auto", stream=None) -> None:
+    """ncz_flash_fwd_static: launch_splits with the partials in the library's
+    static device scratch (no allocation); launches on one device must be ordered."""
+    d = make_desc(q, k, v, o, opts, row_strides=row_strides, producer=producer, stream=stream)
+    _check(lib().ncz_flash_fwd_static(ctypes.byref(d), int(splits)), "flash.launch_static")
 
 
 def launch_host(q_host, k_host, v_host, o_host, q, k, v, o, opts: Options, *, chunk_slices: int = 0,

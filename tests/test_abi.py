@@ -230,3 +230,17 @@ def test_host_pipeline_validates_before_any_device_work(ncz):
     if not torch.cuda.is_available():
         rc = lib.ncz_flash_fwd_host(ctypes.byref(good), 1, 1, 1, 1, 0)
         assert ncz.flash.STATUS_NAMES[rc] in ("NoDevice", "NotInitialized", "NotFound", "UnknownError")
+
+
+def test_split_entry_points_validate(ncz):
+    lib = ncz.flash.lib()
+    D = ncz.flash._Desc
+    st = 64 * 16
+    good = D(q=1, k=1, v=1, o=1, batch_heads=2, seq_len=64, head_dim=16, q_stride=st, k_stride=st, v_stride=st,
+             o_stride=st, scale=0.25, causal=1, o_dtype=0, producer=0, device=-1, stream=None)
+    for fn in (lib.ncz_flash_fwd_splits, lib.ncz_flash_fwd_static):
+        assert ncz.flash.STATUS_NAMES[fn(None, 0)] == "InvalidValue"
+        assert ncz.flash.STATUS_NAMES[fn(ctypes.byref(good), -1)] == "InvalidValue"
+        bad = D.from_buffer_copy(good)
+        bad.seq_len = 0
+        assert ncz.flash.STATUS_NAMES[fn(ctypes.byref(bad), 2)] == "InvalidValue"

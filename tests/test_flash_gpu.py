@@ -330,3 +330,54 @@ def test_split_kv_repeated_launches_and_streams(ncz, oracle_mod):
         side.synchronize()
         assert np.array_equal(o.cpu().numpy(), first)
     assert ncz.sync_status() == 0
+
+
+def _dev_inputs(p):
+    dev = torch.device("cuda:0")
+    q, k, v = (torch.from_numpy(a).to(dev) for a in (p.q, p.k, p.v))
+    opts = C_opts(p)
+    return q, k, v, opts
+
+
+def C_opts(p):
+    import importlib
+
+    ncz = importlib.import_module("not-cute-zig_b200")
+    return ncz.Options(seq_len=p.seq, head_dim=p.d, q_stride=p.strides[0], k_stride=p.strides[1],
+                       v_stride=p.strides[2], o_stride=p.strides[3], scale=p.scale, batch_heads=p.bh,
+                       causal=p.causal)
+
+
+def _out(p, dtype=torch.float32):
+    return torch.full((p.bh * p.strides[3],), SENTINEL, dtype=dtype, device=torch.device("cuda:0"))
+
+
+def test_static_scratch_entry_matches_pool_path(ncz, oracle_mod):
+    """ncz_flash_fwd_static (partials in the static device scratch, no allocation)
+    gives the pool path's bits when the same split count fits, and the oracle's values."""
+    p = C.normal_problem(1, 4096, 64, True, 5, oracle_mod, std=0.7)
+    q, k, v, opts = _dev_inputs(p)
+    a, b = _out(p), _out(p)
+    before = ncz.flash.launch_count()
+    ncz.launch_static(q, k, v, a, opts, 0)
+    assert ncz.flash.launch_count() - before == 2  # split forward + combine
+    ncz.launch_splits(q, k, v, b, opts, 0)
+    assert ncz.sync_status() == 0
+    assert torch.equal(a, b)
+    C.check(a.cpu().numpy(), C.reference(p, oracle_mod), C.active_index(p), "static scratch bh=1 S=4096")
+
+
+@pytest.mark.parametrize("bh,splits,expect", [(2, 4, 3), (4, 8, 1)])
+def test_static_scratch_lowers_the_split_count_to_fit(ncz, oracle_mod, bh, splits, expect):
+    """16 MiB of scratch holds 4 Mi floats: at S=8192, d=64 one split of bh slices
+    needs bh*8192*66 floats, so bh=2 runs 3 splits and bh=4 runs unsplit; the
+    results equal the pool path run with that split count, bit for bit."""
+    p = C.normal_problem(bh, 8192, 64, True, 13, oracle_mod, std=0.7)
+    q, k, v, opts = _dev_inputs(p)
+    a, b = _out(p), _out(p)
+    before = ncz.flash.launch_count()
+    ncz.launch_static(q, k, v, a, opts, splits)
+    assert ncz.flash.launch_count() - before == (2 if expect > 1 else 1)
+    ncz.launch_splits(q, k, v, b, opts, expect)
+    assert ncz.sync_status() == 0
+    assert torch.equal(a, b)
