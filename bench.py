@@ -253,6 +253,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--splits", type=int, default=None,
+                    help="force the split-KV count (ncz_flash_fwd_splits: 1 = none); default: automatic")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -305,7 +307,9 @@ def main():
         torch.cuda.synchronize(dev)
 
     def step():
-        if o_dtype == "f16":
+        if args.splits is not None:
+            ncz.launch_splits(q, k, v, o, opts, args.splits, stream=stream)
+        elif o_dtype == "f16":
             ncz.launch_ex(q, k, v, o, opts, stream=stream)
         else:
             ncz.launch(q, k, v, o, opts, stream=stream)
@@ -394,7 +398,7 @@ def main():
             "vs_baseline": None, "dtype": "f16", "data": "synthetic",
             "config": {"workload": desc, "batch_heads_per_gpu": bh, "batch_heads_total": bh * world,
                        "seq_len": s, "head_dim": d, "causal": causal, "o_dtype": o_dtype,
-                       "parallelism": f"slices sharded x{world}, no collective",
+                       "parallelism": f"slices sharded x{world}, no collective", "split_kv": "auto" if args.splits is None else args.splits,
                        "l2": ("inputs 3x%.1f MB + O %.1f MB > 126 MB L2; no flush" if flush is None else
                               "inputs 3x%.1f MB + O %.1f MB fit in L2: 256 MB memset before every timed step, "
                               "outside the timed intervals") % (n * 2 / 1e6, n * o.element_size() / 1e6)},
