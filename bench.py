@@ -134,6 +134,33 @@ def make_inputs(oracle, bh, s, d, std, k_mul, seed):
 # ---------------------------------------------------------------------------
 # CPU leg: the oracle (restated reference CPU attention) on a bounded sample
 # ---------------------------------------------------------------------------
+def host_threads(oracle):
+    """All host threads this process may run on (torchrun sets OMP_NUM_THREADS=1
+    for its workers; the CPU legs use every core they are allowed)."""
+    try:
+        n = len(os.sched_getaffinity(0))
+    except AttributeError:
+        n = os.cpu_count() or 1
+    return max(n, oracle.max_threads())
+
+
+class _StdoutToStderr:
+    """Sends C-level writes to stdout (the NCCL version banner) to stderr, so
+    rank 0's stdout carries only the JSON line."""
+
+    def __enter__(self):
+        sys.stdout.flush()
+        self.saved = os.dup(1)
+        os.dup2(2, 1)
+        return self
+
+    def __exit__(self, *exc):
+        sys.stdout.flush()
+        os.dup2(self.saved, 1)
+        os.close(self.saved)
+        return False
+
+
 def cpu_sample(oracle, q, k, v, s, d, causal, scale, target_s, threads=0, bh=1):
     """Times the oracle on a bounded sample of the workload sized to about
     target_s seconds: the last rows of slice 0 (the heaviest rows under causal
@@ -141,7 +168,7 @@ def cpu_sample(oracle, q, k, v, s, d, causal, scale, target_s, threads=0, bh=1):
     (TFLOP/s, seconds, description, flops, threads)."""
     import numpy as np
 
-    threads = threads or oracle.max_threads()
+    threads = threads or host_threads(oracle)
 
     def run_rows(rows):
         out = np.zeros(s * d, dtype=np.float32)
@@ -201,7 +228,7 @@ def reference_arm(args):
     bh, s, d, causal, std, k_mul, seed, o_dtype, desc = WORKLOADS[args.workload]
     q, k, v = make_inputs(oracle, 1, s, d, std, k_mul, seed)
     scale = 1.0 / math.sqrt(d)
-    threads = oracle.max_threads()
+    threads = host_threads(oracle)
     budget = 90.0  # seconds of CPU work for the whole --steps/--warmup run
     _, dt_cal, _, _, _, rows_cal = cpu_sample(oracle, q, k, v, s, d, causal, scale, 1.0, threads)
     per_row = dt_cal / rows_cal
@@ -280,7 +307,9 @@ def main():
 
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        with _StdoutToStderr():
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+            dist.barrier()
 
     bh, s, d, causal, std, k_mul, seed, o_dtype, desc = WORKLOADS[args.workload]
     scale = 1.0 / math.sqrt(d)

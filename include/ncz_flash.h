@@ -174,6 +174,19 @@ int ncz_flash_fwd_host(const ncz_flash_desc *desc, const void *q_host, const voi
  * receives the raw status word (0 if clean). */
 int ncz_flash_sync_status(int device, void *stream, uint32_t *detail);
 
+/* --- Test hooks for the failure-detection path (device work, no fault). --- */
+
+/* Bound of every in-kernel mbarrier wait on `device` (-1 = current), in SM
+ * cycles; 0 restores the default (4e9, about 2 s).  A test shortens it so an
+ * expired wait is seen quickly. */
+int ncz_test_set_wait_limit(int device, uint64_t cycles);
+
+/* enable != 0: in every following launch on `device`, the MMA warp of the
+ * first Q tile never signals its first scores, so that tile's softmax wait
+ * runs out, the CTA aborts cleanly and ncz_flash_sync_status reports
+ * NCZ_ERROR_DEVICE_TIMEOUT.  enable = 0 restores normal operation. */
+int ncz_test_drop_arrive(int device, int enable);
+
 /* Human-readable name of a status code (static storage). */
 const char *ncz_status_string(int status);
 

@@ -645,6 +645,34 @@ int ncz_flash_sync_status(int device, void *stream, uint32_t *detail) {
     return word != 0 ? NCZ_ERROR_DEVICE_TIMEOUT : NCZ_SUCCESS;
 }
 
+int ncz_test_set_wait_limit(int device, uint64_t cycles) {
+    int st = ncz_init();
+    if (st != NCZ_SUCCESS) return st;
+    int prev = 0;
+    cudaError_t e = cudaGetDevice(&prev);
+    if (e != cudaSuccess) return map_cuda_error(e);
+    const int dev = device >= 0 ? device : prev;
+    if (dev != prev && (e = cudaSetDevice(dev)) != cudaSuccess) return map_cuda_error(e);
+    const unsigned long long v = cycles != 0 ? cycles : ncz::kWaitLimitCycles;
+    e = cudaMemcpyToSymbol(ncz::g_ncz_wait_limit, &v, sizeof(v));
+    if (dev != prev) cudaSetDevice(prev);
+    return e == cudaSuccess ? NCZ_SUCCESS : map_cuda_error(e);
+}
+
+int ncz_test_drop_arrive(int device, int enable) {
+    int st = ncz_init();
+    if (st != NCZ_SUCCESS) return st;
+    int prev = 0;
+    cudaError_t e = cudaGetDevice(&prev);
+    if (e != cudaSuccess) return map_cuda_error(e);
+    const int dev = device >= 0 ? device : prev;
+    if (dev != prev && (e = cudaSetDevice(dev)) != cudaSuccess) return map_cuda_error(e);
+    const int v = enable != 0;
+    e = cudaMemcpyToSymbol(ncz::g_ncz_test_drop, &v, sizeof(v));
+    if (dev != prev) cudaSetDevice(prev);
+    return e == cudaSuccess ? NCZ_SUCCESS : map_cuda_error(e);
+}
+
 const char *ncz_status_string(int status) {
     switch (status) {
         case NCZ_SUCCESS: return "Success";

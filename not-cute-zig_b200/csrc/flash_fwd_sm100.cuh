@@ -31,7 +31,7 @@
 // rescaled in TMEM only when the row max grows by more than 2^8 since the
 // last rescale (P <= 2^8 then still fits f16, and O / l is unchanged).
 //
-// Every mbarrier wait is bounded (kWaitLimitCycles).  On expiry the waiter
+// Every mbarrier wait is bounded (g_ncz_wait_limit cycles).  On expiry the waiter
 // records where it gave up in g_ncz_status, raises a CTA-wide abort flag and
 // all roles leave their loops; issued copies and MMAs are waited for
 // (bounded) before TMEM is freed and the CTA exits.  No trap, no assert.
@@ -55,7 +55,7 @@ constexpr uint32_t kTileCols = kColO + 64;
 static_assert(kQTiles * kTileCols <= kTmemCols, "TMEM budget");
 constexpr float kRescaleThreshold = 8.0f;                   // log2 units
 constexpr float kMaxP = 256.0f;                             // 2^kRescaleThreshold
-// Spin-wait bound in SM cycles (about 2 s at 2 GHz; longer at lower clocks).
+// Default spin-wait bound in SM cycles (about 2 s at 2 GHz; longer at lower clocks).
 constexpr unsigned long long kWaitLimitCycles = 4000000000ull;
 // Exponentials: in every group of kExp2EmuPeriod column pairs, the last
 // kExp2EmuCount pairs are computed by a polynomial on the FMA pipe instead of
@@ -159,6 +159,11 @@ struct Work {
 };
 
 __device__ uint32_t g_ncz_status = 0u;
+// Bound of every mbarrier wait, in SM cycles (tests shorten it, ncz_test_set_wait_limit).
+__device__ unsigned long long g_ncz_wait_limit = kWaitLimitCycles;
+// Test hook (ncz_test_drop_arrive): when set, the MMA warp of Q tile 0 never
+// signals its first scores, so the softmax's bounded wait runs out.
+__device__ int g_ncz_test_drop = 0;
 
 __device__ __forceinline__ Work make_work(const FlashParams &p) {
     Work wk;
@@ -188,7 +193,7 @@ __device__ __forceinline__ Work make_work(const FlashParams &p) {
 }
 
 // Bounded mbarrier wait.  Returns false when the CTA is aborting or the wait
-// exceeded kWaitLimitCycles (then it raises the abort flag and records the site).
+// exceeded g_ncz_wait_limit (then it raises the abort flag and records the site).
 // honor_abort = false is used by teardown waits that must not be skipped.
 // The slow loop is out of line; the common already-complete case costs one
 // inlined try_wait.
@@ -199,7 +204,7 @@ __device__ __noinline__ bool bounded_wait_slow(uint32_t bar, uint32_t parity, vo
         if (mbar_try_wait(bar, parity)) return true;
         if ((it & 15u) == 0u) {
             if (honor_abort && *abort_flag) return false;
-            if (sm_clock() - t0 > kWaitLimitCycles) {
+            if (sm_clock() - t0 > g_ncz_wait_limit) {
                 *abort_flag = 1u;
                 atomicCAS(&g_ncz_status, 0u, 0x80000000u | (site << 24) | (blockIdx.x & 0xFFFFFFu));
                 return false;
@@ -228,7 +233,7 @@ __device__ __forceinline__ bool warp_wait_inline(uint32_t bar, uint32_t parity, 
             }
             if ((it & 15u) == 0u) {
                 if (*abort_flag) break;
-                if (sm_clock() - t0 > kWaitLimitCycles) {
+                if (sm_clock() - t0 > g_ncz_wait_limit) {
                     *abort_flag = 1u;
                     atomicCAS(&g_ncz_status, 0u, 0x80000000u | (site << 24) | (blockIdx.x & 0xFFFFFFu));
                     break;
@@ -421,7 +426,7 @@ __device__ __forceinline__ void mma_role(int w, uint32_t sbase, uint32_t tmem, c
         if (ok) {
             tc_fence_after();
             issue_qk<D>(0, sbase, tS, qdesc);
-            umma_commit_elect(b.s_full(w));
+            if (!(w == 0 && g_ncz_test_drop != 0)) umma_commit_elect(b.s_full(w));
         }
     }
     int j = 0;

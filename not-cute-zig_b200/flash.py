@@ -111,6 +111,8 @@ _SIGNATURES = {
     "ncz_flash_fwd_splits": (ctypes.c_int, [ctypes.POINTER(_Desc), ctypes.c_int]),
     "ncz_flash_fwd_static": (ctypes.c_int, [ctypes.POINTER(_Desc), ctypes.c_int]),
     "ncz_flash_sync_status": (ctypes.c_int, [ctypes.c_int, _VP, ctypes.POINTER(ctypes.c_uint32)]),
+    "ncz_test_set_wait_limit": (ctypes.c_int, [ctypes.c_int, ctypes.c_uint64]),
+    "ncz_test_drop_arrive": (ctypes.c_int, [ctypes.c_int, ctypes.c_int]),
     "ncz_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "ncz_launch_count": (ctypes.c_uint64, []),
     "ncz_umma_smem_desc": (ctypes.c_uint64, [ctypes.c_uint32] * 4),

@@ -381,3 +381,32 @@ def test_static_scratch_lowers_the_split_count_to_fit(ncz, oracle_mod, bh, split
     ncz.launch_splits(q, k, v, b, opts, expect)
     assert ncz.sync_status() == 0
     assert torch.equal(a, b)
+
+
+def test_expired_wait_reports_device_timeout_and_context_survives(ncz, oracle_mod):
+    """Failure detection without a GPU fault: with a short wait limit and the
+    first scores never signalled (a barrier that nothing completes), the CTA
+    aborts cleanly, ncz_flash_sync_status returns DeviceTimeout with the wait
+    site (s_full = 5) in the status word, and the same context then runs a
+    correct launch."""
+    import ctypes
+
+    lib = ncz.flash.lib()
+    p = C.normal_problem(1, 200, 64, True, 3, oracle_mod, std=0.6)
+    assert lib.ncz_test_set_wait_limit(-1, 20_000_000) == 0  # about 10 ms
+    assert lib.ncz_test_drop_arrive(-1, 1) == 0
+    try:
+        dev = torch.device("cuda:0")
+        q, k, v = (torch.from_numpy(a).to(dev) for a in (p.q, p.k, p.v))
+        o = torch.full((p.bh * p.strides[3],), SENTINEL, dtype=torch.float32, device=dev)
+        ncz.launch(q, k, v, o, C_opts(p))
+        detail = ctypes.c_uint32(0)
+        rc = lib.ncz_flash_sync_status(-1, None, ctypes.byref(detail))
+        assert ncz.flash.STATUS_NAMES[rc] == "DeviceTimeout"
+        assert detail.value >> 31 == 1 and (detail.value >> 24) & 0x7F == 5
+    finally:
+        assert lib.ncz_test_drop_arrive(-1, 0) == 0
+        assert lib.ncz_test_set_wait_limit(-1, 0) == 0
+    assert ncz.sync_status() == 0  # the word was cleared
+    got = run(ncz, p)
+    C.check(got, C.reference(p, oracle_mod), C.active_index(p), "launch after an expired wait")
