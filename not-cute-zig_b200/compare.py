@@ -1,0 +1,145 @@
+"""Flash-attention compare / benchmark harness with the reference's JSONL records.
+
+Mirrors compareFlash (src/main.zig:975-1041) and benchmarkFlash
+(src/main.zig:790-856): fillFlashInput inputs (src/main.zig:1207-1211),
+5 warm-up + 20 timed launches through benchmark.run_kernel, algorithmic
+bytes and FLOPs by the reference formulas (src/main.zig:843-845), and one
+JSONL record per shape in the reference's field order (src/main.zig:873-881)
+plus gpus, device_ms, pct_peak_nominal, pct_peak_measured, max_rel_error,
+host_cores and label.  Correctness is checked against plain fp32 attention in
+torch on the same device (max-abs <= 0.02, the reference's compare bound,
+src/main.zig:1042); rel = |a - b| / max(|b|, 1e-3).
+
+    python not-cute-zig_b200/compare.py                  # the 15 reference shapes
+    python not-cute-zig_b200/compare.py --shape 8,1024,64,1 --gpus 2 --jsonl out.jsonl
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import math
+import os
+import sys
+from typing import List, Optional, Tuple
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+if os.path.dirname(_HERE) not in sys.path:
+    sys.path.insert(0, os.path.dirname(_HERE))
+
+# compareFlash calls, src/main.zig:141-170: (batch_heads, seq_len, head_dim, causal)
+REFERENCE_SHAPES: List[Tuple[int, int, int, bool]] = [
+    (2, 32, 16, False), (2, 32, 32, True), (2, 64, 16, False), (2, 64, 32, True), (2, 128, 32, True),
+    (8, 128, 16, False), (8, 128, 32, True), (8, 256, 16, False), (8, 256, 32, True), (16, 256, 32, False),
+    (16, 512, 32, True), (8, 256, 64, False), (8, 512, 64, True), (16, 512, 64, False), (8, 1024, 64, True),
+]
+NOMINAL_F16_TFLOPS = 2250.0
+
+
+def fill_flash_input(n: int, mul: int, add: int, scale: float):
+    """fillFlashInput: f16(((i * mul + add) % 17) * scale), src/main.zig:1207-1211."""
+    import numpy as np
+
+    i = np.arange(n, dtype=np.int64)
+    return (((i * mul + add) % 17).astype(np.float32) * np.float32(scale)).astype(np.float16)
+
+
+def torch_attention(q, k, v, bh: int, s: int, d: int, scale: float, causal: bool):
+    """fp32 attention in torch (cross-check only): softmax(QK^T * scale, causal
+    top-left) V, per slice."""
+    import torch
+
+    qf, kf, vf = (t.view(bh, s, d).float() for t in (q, k, v))
+    scores = torch.matmul(qf, kf.transpose(1, 2)) * scale
+    if causal:
+        mask = torch.ones(s, s, dtype=torch.bool, device=q.device).triu(1)
+        scores = scores.masked_fill(mask, float("-inf"))
+    return torch.matmul(torch.softmax(scores, dim=-1), vf).reshape(-1)
+
+
+def measured_peak() -> Optional[float]:
+    path = os.path.join(os.path.dirname(_HERE), "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["bf16_tflops"])
+    except (OSError, KeyError, ValueError):
+        return None
+
+
+def compare_shape(ncz, bh: int, s: int, d: int, causal: bool, gpus: int = 1) -> dict:
+    import torch
+
+    from importlib import import_module
+
+    bench = import_module("not-cute-zig_b200.benchmark")
+    shard = import_module("not-cute-zig_b200.shard")
+    stride = s * d
+    n = bh * stride
+    scale = 1.0 / math.sqrt(d)
+    hq, hk, hv = fill_flash_input(n, 3, 1, 0.125), fill_flash_input(n, 5, 2, 0.0625), fill_flash_input(n, 7, 3, 0.03125)
+    flops = bh * (4 * ((s * (s + 1)) // 2 if causal else s * s) * d)
+    bytes_ = n * (2 * 3 + 4)
+    gpus = max(1, min(gpus, torch.cuda.device_count(), bh))
+    launches, streams, outs = [], [], []
+    for g in range(gpus):
+        lo, hi = shard.slice_range(bh, gpus, g)
+        dev = torch.device("cuda", g)
+        q = torch.from_numpy(hq[lo * stride:hi * stride]).to(dev)
+        k = torch.from_numpy(hk[lo * stride:hi * stride]).to(dev)
+        v = torch.from_numpy(hv[lo * stride:hi * stride]).to(dev)
+        o = torch.zeros((hi - lo) * stride, dtype=torch.float32, device=dev)
+        st = torch.cuda.Stream(dev)
+        opts = ncz.Options(seq_len=s, head_dim=d, q_stride=stride, k_stride=stride, v_stride=stride,
+                           o_stride=stride, scale=scale, batch_heads=hi - lo, causal=causal)
+        launches.append(lambda q=q, k=k, v=v, o=o, opts=opts, st=st: ncz.launch(q, k, v, o, opts, stream=st))
+        streams.append(st)
+        outs.append((q, k, v, o, lo, hi))
+    if gpus == 1:
+        res = bench.run_kernel(launches[0], warmup_iters=5, iters=20, bytes_processed=bytes_,
+                               flops_processed=flops, stream=streams[0])
+        res.device_ms = [res.mean_ms]
+    else:
+        res = bench.run_multi(launches, streams, warmup_iters=5, iters=20, bytes_processed=bytes_,
+                              flops_processed=flops)
+    max_abs, max_rel = 0.0, 0.0
+    for (q, k, v, o, lo, hi), st in zip(outs, streams):
+        st.synchronize()
+        ncz.sync_status(device=q.device.index, stream=st)
+        want = torch_attention(q, k, v, hi - lo, s, d, scale, causal)
+        diff = (o - want).abs()
+        max_abs = max(max_abs, float(diff.max()))
+        max_rel = max(max_rel, float((diff / want.abs().clamp_min(1e-3)).max()))
+    peak = measured_peak()
+    shape = f"batch_heads={bh},seq={s},head={d},causal={str(causal).lower()}"
+    label = ncz.select_kernel(ncz.Options(seq_len=s, head_dim=d, q_stride=stride, k_stride=stride,
+                                          v_stride=stride, o_stride=stride, scale=scale, batch_heads=bh,
+                                          causal=causal)).label
+    return res.record("flash_attention", "not_cute_zig_b200", shape, max_abs <= 0.02, bytes_, flops, max_abs,
+                      gpus=gpus, device_ms=res.device_ms, host_ms=res.host_ms,
+                      pct_peak_nominal=(res.tflops or 0.0) / NOMINAL_F16_TFLOPS,
+                      pct_peak_measured=((res.tflops or 0.0) / peak) if peak else None,
+                      max_rel_error=max_rel, host_cores=bench.host_cores(), label=label)
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--shape", action="append", default=[],
+                    help="bh,seq,head,causal (repeatable); default: the 15 reference compare shapes")
+    ap.add_argument("--gpus", type=int, default=1, help="shard slices across this many devices")
+    ap.add_argument("--jsonl", default=None, help="append records to this file instead of stdout")
+    args = ap.parse_args(argv)
+    ncz = importlib.import_module("not-cute-zig_b200")
+    bench = importlib.import_module("not-cute-zig_b200.benchmark")
+    shapes = REFERENCE_SHAPES
+    if args.shape:
+        shapes = []
+        for spec in args.shape:
+            bh, s, d, c = (int(x) for x in spec.split(","))
+            shapes.append((bh, s, d, bool(c)))
+    records = [compare_shape(ncz, bh, s, d, c, args.gpus) for bh, s, d, c in shapes]
+    bench.emit(records, args.jsonl)
+    return 0 if all(r["correct"] for r in records) else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -216,22 +216,26 @@ def launch(q, k, v, o, opts: Options, stream=None) -> None:
     """flash.launch (src/flash.zig:31-70): validate, requireLen, launch (async).
 
     q/k/v: float16 CUDA tensors, o: float32 CUDA tensor, each holding at least
-    batch_heads * stride elements.
+    batch_heads * stride elements.  The C call launches on the current device,
+    so q's device is made current for it (tensors carry their device here).
     """
+    import torch
+
     _require(q, "float16", "q")
     _require(k, "float16", "k")
     _require(v, "float16", "v")
     _require(o, "float32", "o")
-    _check(
-        lib().ncz_flash_launch(
+    if not (k.device == v.device == o.device == q.device):
+        raise FlashError(5, "q, k, v and o must be on one device")
+    with torch.cuda.device(q.device):
+        status = lib().ncz_flash_launch(
             q.data_ptr(), q.numel(), k.data_ptr(), k.numel(), v.data_ptr(), v.numel(),
             o.data_ptr(), o.numel(),
             opts.batch_heads, opts.seq_len, opts.head_dim,
             opts.q_stride, opts.k_stride, opts.v_stride, opts.o_stride,
             float(opts.scale), int(bool(opts.causal)), _stream_handle(stream),
-        ),
-        "flash.launch",
-    )
+        )
+    _check(status, "flash.launch")
 
 
 def make_desc(q, k, v, o, opts: Options, *, row_strides: Optional[Sequence[int]] = None,

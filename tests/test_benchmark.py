@@ -1,0 +1,57 @@
+"""benchmark.py / compare.py host logic on the CPU: the reference's rate
+formulas (src/benchmark.zig:79-86), the compare record schema
+(src/main.zig:873-881) and fillFlashInput (src/main.zig:1207-1211)."""
+import importlib
+import json
+
+import numpy as np
+import pytest
+
+
+@pytest.fixture(scope="module")
+def bench():
+    return importlib.import_module("not-cute-zig_b200.benchmark")
+
+
+@pytest.fixture(scope="module")
+def compare():
+    return importlib.import_module("not-cute-zig_b200.compare")
+
+
+def test_summarize_rates_follow_the_reference_formulas(bench):
+    r = bench.summarize([2.0, 1.0, 3.0], bytes_processed=4_000_000_000, flops_processed=6_000_000_000_000)
+    assert (r.mean_ms, r.min_ms, r.max_ms) == (2.0, 1.0, 3.0)
+    assert r.throughput_gbps == pytest.approx(4e9 / (2.0 * 1e6))  # 2000 GB/s
+    assert r.tflops == pytest.approx(6e12 / (2.0 * 1e9))          # 3000 TFLOP/s
+    assert bench.summarize([1.0]).tflops is None
+    with pytest.raises(ValueError):
+        bench.summarize([])
+
+
+def test_record_keeps_the_reference_field_order(bench):
+    r = bench.summarize([1.5], bytes_processed=10, flops_processed=20)
+    rec = r.record("flash_attention", "not_cute_zig_b200", "batch_heads=2,seq=32,head=16,causal=false", True, 10, 20,
+                   1e-4, gpus=1, max_rel_error=2e-3)
+    keys = list(rec)
+    assert keys[:12] == ["kernel", "implementation", "shape", "correct", "mean_ms", "min_ms", "max_ms", "gbps",
+                         "tflops", "bytes", "flops", "max_abs_error"]
+    assert rec["gpus"] == 1 and rec["max_rel_error"] == 2e-3
+    json.dumps(rec)
+
+
+def test_emit_writes_jsonl(bench, tmp_path):
+    p = tmp_path / "out.jsonl"
+    bench.emit([{"a": 1}, {"b": 2}], str(p))
+    assert [json.loads(x) for x in p.read_text().splitlines()] == [{"a": 1}, {"b": 2}]
+
+
+def test_fill_flash_input_matches_the_oracle(compare, oracle_mod):
+    for mul, add, scale in ((3, 1, 0.125), (5, 2, 0.0625), (7, 3, 0.03125)):
+        assert np.array_equal(compare.fill_flash_input(1000, mul, add, scale),
+                              oracle_mod.fill_pattern(1000, mul, add, scale))
+
+
+def test_reference_shape_list(compare):
+    from tests import cases as C
+
+    assert compare.REFERENCE_SHAPES == C.COMPARE_CASES

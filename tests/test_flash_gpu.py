@@ -410,3 +410,27 @@ def test_expired_wait_reports_device_timeout_and_context_survives(ncz, oracle_mo
     assert ncz.sync_status() == 0  # the word was cleared
     got = run(ncz, p)
     C.check(got, C.reference(p, oracle_mod), C.active_index(p), "launch after an expired wait")
+
+
+def test_compare_harness_records(ncz):
+    """compare.py (the reference's compareFlash + JSONL record) on three of the
+    reference shapes: correct against fp32 torch attention, rates consistent."""
+    import importlib
+
+    compare = importlib.import_module("not-cute-zig_b200.compare")
+    for bh, s, d, causal in ((2, 32, 16, False), (8, 256, 32, True), (8, 1024, 64, True)):
+        rec = compare.compare_shape(ncz, bh, s, d, causal)
+        assert rec["correct"] and rec["max_abs_error"] <= 2e-3
+        assert rec["tflops"] == pytest.approx(rec["flops"] / (rec["mean_ms"] * 1e9))
+        assert rec["min_ms"] <= rec["mean_ms"] <= rec["max_ms"] and rec["gpus"] == 1
+        assert rec["label"] == f"flash_fwd_sm100a_d{d}"
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_compare_harness_multi_device(ncz):
+    import importlib
+
+    compare = importlib.import_module("not-cute-zig_b200.compare")
+    rec = compare.compare_shape(ncz, 8, 1024, 64, True, gpus=2)
+    assert rec["correct"] and rec["gpus"] == 2 and len(rec["device_ms"]) == 2
+    assert rec["mean_ms"] >= max(rec["device_ms"]) - 1e-6  # the slowest device per iteration
