@@ -156,7 +156,8 @@ int ncz_flash_fwd_multi(const ncz_flash_desc *descs, int count);
  * o_host are HOST buffers laid out exactly like desc->q/k/v/o (same strides);
  * desc->q/k/v/o are caller-owned device buffers of the same layout that stage
  * them.  Slices are processed in chunks of chunk_slices (0 = bh/8 rounded up,
- * but at least 4 MiB of Q/K/V per chunk):
+ * but at least 4 MiB of Q/K/V per chunk, the first two and last two chunks a
+ * quarter and a half of that):
  * a chunk's Q/K/V upload, its forward and its O download run on separate
  * streams, so the upload of chunk i+1 overlaps the forward of chunk i and the
  * download of chunk i-1.  Host buffers must be page-locked (pinned) for the

@@ -19,6 +19,7 @@
 #include <cstdint>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "flash_fwd_sm100.cuh"
 #include "ncz_flash.h"
@@ -412,8 +413,30 @@ size_t chunk_elems(size_t s0, size_t s1, size_t slice, size_t row, size_t seq, s
     return (s1 - s0 - 1) * slice + (seq - 1) * row + d;
 }
 
+// Chunk sizes (slices) covering bh: `chunk` each, or with taper the first and
+// last two chunks a quarter and a half of it, so the first forward starts and
+// the last download ends sooner (only one PCIe direction is busy then).
+std::vector<size_t> chunk_plan(size_t bh, size_t chunk, bool taper) {
+    std::vector<size_t> plan;
+    const size_t a = std::max<size_t>(1, chunk / 4), b = std::max<size_t>(1, chunk / 2);
+    if (taper && chunk >= 4 && bh >= 2 * (a + b) + chunk) {
+        plan = {a, b};
+        size_t mid = bh - 2 * (a + b);
+        while (mid > 0) {
+            const size_t c = std::min(chunk, mid);
+            plan.push_back(c);
+            mid -= c;
+        }
+        plan.push_back(b);
+        plan.push_back(a);
+    } else {
+        for (size_t s0 = 0; s0 < bh; s0 += chunk) plan.push_back(std::min(chunk, bh - s0));
+    }
+    return plan;
+}
+
 int host_pipeline(const Resolved &r, const void *qh, const void *kh, const void *vh, void *oh, size_t chunk,
-                  int dev) {
+                  bool taper, int dev) {
     HostPipe &hp = g_pipes[dev];
     std::lock_guard<std::mutex> lock(hp.mu);
     int st = pipe_setup(hp);
@@ -423,8 +446,9 @@ int host_pipeline(const Resolved &r, const void *qh, const void *kh, const void 
     if (e == cudaSuccess) e = cudaStreamWaitEvent(hp.up, hp.fork, 0);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(hp.down, hp.fork, 0);
     if (e != cudaSuccess) return map_cuda_error(e);
-    for (size_t s0 = 0; s0 < r.bh; s0 += chunk) {
-        const size_t s1 = s0 + chunk < r.bh ? s0 + chunk : r.bh;
+    size_t s0 = 0;
+    for (const size_t n_slices : chunk_plan(r.bh, chunk, taper)) {
+        const size_t s1 = s0 + n_slices;
         struct Op {
             const void *dev;
             const void *host;
@@ -456,6 +480,7 @@ int host_pipeline(const Resolved &r, const void *qh, const void *kh, const void 
                                 chunk_elems(s0, s1, r.os, r.orow, r.seq, r.d) * osz, cudaMemcpyDeviceToHost, hp.down);
         }
         if (e != cudaSuccess) return map_cuda_error(e);
+        s0 = s1;
     }
     e = cudaEventRecord(hp.join, hp.down);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(r.stream, hp.join, 0);
@@ -611,14 +636,15 @@ int ncz_flash_fwd_host(const ncz_flash_desc *desc, const void *q_host, const voi
         if (e != cudaSuccess) return map_cuda_error(e);
     }
     // Default: 8 chunks, so one chunk's upload hides the previous chunk's forward,
-    // but at least 4 MiB of Q/K/V per chunk (smaller copies cost more than they hide).
+    // but at least 4 MiB of Q/K/V per chunk (smaller copies cost more than they
+    // hide), with tapered first and last chunks.
     size_t chunk = chunk_slices;
     if (chunk == 0) {
         const size_t slice_bytes = (r.qs + r.ks + r.vs) * 2;
         const size_t min_slices = ((size_t(4) << 20) + slice_bytes - 1) / slice_bytes;
         chunk = std::max((r.bh + 7) / 8, min_slices);
     }
-    st = host_pipeline(r, q_host, k_host, v_host, o_host, chunk, dev);
+    st = host_pipeline(r, q_host, k_host, v_host, o_host, chunk, chunk_slices == 0, dev);
     if (dev != prev) cudaSetDevice(prev);
     return st;
 }

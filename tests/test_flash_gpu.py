@@ -434,3 +434,24 @@ def test_compare_harness_multi_device(ncz):
     rec = compare.compare_shape(ncz, 8, 1024, 64, True, gpus=2)
     assert rec["correct"] and rec["gpus"] == 2 and len(rec["device_ms"]) == 2
     assert rec["mean_ms"] >= max(rec["device_ms"]) - 1e-6  # the slowest device per iteration
+
+
+def test_host_pipeline_tapered_default_matches_device_launch(ncz, oracle_mod):
+    """bh=96, S=1024: the default plan tapers (3, 6, 12 x 6, 6, 6, 3 slices); the
+    result equals the device path bit for bit."""
+    bh, s, d = 96, 1024, 64
+    p = C.normal_problem(bh, s, d, True, 67, oracle_mod, std=0.7)
+    dev = torch.device("cuda:0")
+    q, k, v = (torch.from_numpy(a).to(dev) for a in (p.q, p.k, p.v))
+    opts = C_opts(p)
+    o_ref = torch.empty(bh * s * d, dtype=torch.float32, device=dev)
+    ncz.launch(q, k, v, o_ref, opts)
+    qh, kh, vh = (torch.from_numpy(a).pin_memory() for a in (p.q, p.k, p.v))
+    oh = torch.full((bh * s * d,), SENTINEL, dtype=torch.float32).pin_memory()
+    qd, kd, vd, od = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v), torch.empty_like(o_ref)
+    before = ncz.flash.launch_count()
+    ncz.launch_host(qh, kh, vh, oh, qd, kd, vd, od, opts)
+    torch.cuda.synchronize()
+    assert ncz.flash.launch_count() - before == 11
+    assert ncz.sync_status() == 0
+    assert torch.equal(oh, o_ref.cpu())
