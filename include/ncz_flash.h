@@ -48,8 +48,10 @@ typedef enum ncz_status {
     NCZ_ERROR_MISALIGNED = 18
 } ncz_status;
 
-/* Output element type. */
-typedef enum ncz_dtype { NCZ_DTYPE_F32 = 0, NCZ_DTYPE_F16 = 1 } ncz_dtype;
+/* Element types: O is f32, f16 or bf16; Q/K/V are f16 or bf16.  With bf16
+ * inputs P is rounded to bf16 before PV (a tensor-core MMA takes A and B of one
+ * type). */
+typedef enum ncz_dtype { NCZ_DTYPE_F32 = 0, NCZ_DTYPE_F16 = 1, NCZ_DTYPE_BF16 = 2 } ncz_dtype;
 
 /* Producer selection: AUTO picks the TMA path when every Q/K/V base pointer is
  * 16-byte aligned and every Q/K/V stride is a multiple of 8 elements, and the
@@ -82,6 +84,7 @@ typedef struct ncz_flash_desc {
     int32_t producer; /* ncz_producer */
     int32_t device;   /* CUDA ordinal, -1 = current */
     void *stream;     /* cudaStream_t / CUstream, NULL = default stream */
+    int32_t in_dtype; /* Q/K/V type: NCZ_DTYPE_F16 (or 0) or NCZ_DTYPE_BF16 */
 } ncz_flash_desc;
 
 /* Loads nothing eagerly; resolves the driver entry points and records the
@@ -207,6 +210,8 @@ uint64_t ncz_umma_smem_desc(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo
 /* tcgen05 kind::f16 instruction descriptor: f16 A/B, f32 accumulate, given
  * M, N and operand majors (0 = K-major, 1 = MN-major). */
 uint32_t ncz_umma_instr_desc_f16(uint32_t m, uint32_t n, uint32_t a_major, uint32_t b_major);
+/* The same with bf16 A and B (bits 7..9 and 10..12 = 1). */
+uint32_t ncz_umma_instr_desc_bf16(uint32_t m, uint32_t n, uint32_t a_major, uint32_t b_major);
 
 /* Byte-address swizzle of a TMA SWIZZLE_{32,64,128}B tile: the shared-memory
  * byte offset at which logical byte offset `offset` of a tile with

@@ -31,7 +31,7 @@ using ncz::SmemLayout;
 
 constexpr int kMaxDevices = 64;
 constexpr size_t kGroupRows = static_cast<size_t>(ncz::kBlockM) * ncz::kQTiles;  // Q rows per CTA
-constexpr int kVariants = 6;  // (D in 16/32/64) x (TMA, LSU)
+constexpr int kVariants = 12;  // (D in 16/32/64) x (TMA, LSU) x (f16, bf16 inputs)
 
 std::mutex g_mu;
 bool g_init_done = false;
@@ -73,6 +73,7 @@ struct Resolved {
     float scale;
     uint32_t causal;
     int o_dtype;
+    int in_dtype;  // NCZ_DTYPE_F16 or NCZ_DTYPE_BF16 (0 in a descriptor = f16)
     int producer;
     int device;
     cudaStream_t stream;
@@ -99,7 +100,9 @@ int validate_resolved(const Resolved &r) {
         size_t total;
         if (!mul_ok(slices[i], r.bh, &total)) return NCZ_ERROR_OVERFLOW;
     }
-    if (r.o_dtype != NCZ_DTYPE_F32 && r.o_dtype != NCZ_DTYPE_F16) return NCZ_ERROR_INVALID_VALUE;
+    if (r.o_dtype != NCZ_DTYPE_F32 && r.o_dtype != NCZ_DTYPE_F16 && r.o_dtype != NCZ_DTYPE_BF16)
+        return NCZ_ERROR_INVALID_VALUE;
+    if (r.in_dtype != NCZ_DTYPE_F16 && r.in_dtype != NCZ_DTYPE_BF16) return NCZ_ERROR_INVALID_VALUE;
     if (r.producer < NCZ_PRODUCER_AUTO || r.producer > NCZ_PRODUCER_LSU) return NCZ_ERROR_INVALID_VALUE;
     // Implementation limits of the 32-bit tile / grid indices.
     if (r.seq > (size_t(1) << 30)) return NCZ_ERROR_INVALID_VALUE;
@@ -121,6 +124,7 @@ Resolved from_desc(const ncz_flash_desc &d) {
     r.orow = d.o_row_stride ? d.o_row_stride : d.head_dim;
     r.scale = d.scale; r.causal = d.causal;
     r.o_dtype = d.o_dtype; r.producer = d.producer; r.device = d.device;
+    r.in_dtype = d.in_dtype == 0 ? NCZ_DTYPE_F16 : d.in_dtype;
     r.stream = static_cast<cudaStream_t>(d.stream);
     return r;
 }
@@ -129,25 +133,26 @@ bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) %
 
 // 3-D map over one operand: dims (d, seq, bh), box (d, box_rows, 1), swizzle = row width.
 bool encode_map(CUtensorMap *map, const void *ptr, size_t d, size_t seq, size_t bh, size_t row, size_t slice,
-                uint32_t box_rows) {
+                uint32_t box_rows, bool bf16) {
     cuuint64_t dims[3] = {d, seq, bh};
     cuuint64_t strides[2] = {row * 2, slice * 2};
     cuuint32_t box[3] = {static_cast<cuuint32_t>(d), box_rows, 1u};
     cuuint32_t estr[3] = {1u, 1u, 1u};
     const CUtensorMapSwizzle swz = d == 64 ? CU_TENSOR_MAP_SWIZZLE_128B
                                            : (d == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
-    const CUresult res = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(ptr), dims, strides,
+    const CUresult res = g_encode(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                                  const_cast<void *>(ptr), dims, strides,
                                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return res == CUDA_SUCCESS;
 }
 
-template <int D, bool kTma>
+template <int D, bool kTma, bool kBf16>
 int launch_variant(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv, const FlashParams &p,
                    unsigned grid, int dev, cudaStream_t stream) {
     using L = SmemLayout<D>;
-    auto kernel = ncz::flash_fwd_sm100<D, kTma>;
-    const int vidx = (D == 16 ? 0 : D == 32 ? 1 : 2) * 2 + (kTma ? 0 : 1);
+    auto kernel = ncz::flash_fwd_sm100<D, kTma, kBf16>;
+    const int vidx = ((D == 16 ? 0 : D == 32 ? 1 : 2) * 2 + (kTma ? 0 : 1)) * 2 + (kBf16 ? 1 : 0);
     {
         std::lock_guard<std::mutex> lock(g_mu);
         if (dev >= kMaxDevices) return NCZ_ERROR_INVALID_DEVICE;
@@ -192,6 +197,22 @@ int static_scratch(int dev, float **out) {
     }
     *out = g_scratch_addr[dev];
     return NCZ_SUCCESS;
+}
+
+// One head_dim: forward variant (producer x input type), then the split-KV merge.
+template <int D>
+int launch_d(bool tma, bool bf16, const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorMap &tv,
+             const FlashParams &p, unsigned grid, int dev, cudaStream_t stream) {
+    int st;
+    if (tma) {
+        st = bf16 ? launch_variant<D, true, true>(tq, tk, tv, p, grid, dev, stream)
+                  : launch_variant<D, true, false>(tq, tk, tv, p, grid, dev, stream);
+    } else {
+        st = bf16 ? launch_variant<D, false, true>(tq, tk, tv, p, grid, dev, stream)
+                  : launch_variant<D, false, false>(tq, tk, tv, p, grid, dev, stream);
+    }
+    if (st == NCZ_SUCCESS && p.num_splits > 1) st = launch_combine<D>(p, stream);
+    return st;
 }
 
 // Library-owned stream-ordered memory pool per device for split-KV partials:
@@ -262,9 +283,10 @@ int launch_on_current(const Resolved &r, int dev) {
     std::memset(&tk, 0, sizeof(tk));
     std::memset(&tv, 0, sizeof(tv));
     if (use_tma) {
-        const bool enc = encode_map(&tq, r.q, r.d, r.seq, r.bh, r.qr, r.qs, ncz::kBlockM) &&
-                         encode_map(&tk, r.k, r.d, r.seq, r.bh, r.kr, r.ks, ncz::kBlockN) &&
-                         encode_map(&tv, r.v, r.d, r.seq, r.bh, r.vr, r.vs, ncz::kBlockN);
+        const bool bf = r.in_dtype == NCZ_DTYPE_BF16;
+        const bool enc = encode_map(&tq, r.q, r.d, r.seq, r.bh, r.qr, r.qs, ncz::kBlockM, bf) &&
+                         encode_map(&tk, r.k, r.d, r.seq, r.bh, r.kr, r.ks, ncz::kBlockN, bf) &&
+                         encode_map(&tv, r.v, r.d, r.seq, r.bh, r.vr, r.vs, ncz::kBlockN, bf);
         if (!enc) {
             if (r.producer == NCZ_PRODUCER_TMA) return NCZ_ERROR_MISALIGNED;
             use_tma = false;  // e.g. strides the TMA unit cannot express: plain-load producer
@@ -289,8 +311,8 @@ int launch_on_current(const Resolved &r, int dev) {
     p.num_groups = static_cast<int>((r.seq + kGroupRows - 1) / kGroupRows);
     p.scale_log2 = static_cast<float>(static_cast<double>(r.scale) * 1.4426950408889634);
     p.causal = r.causal != 0;
-    p.o_f16 = r.o_dtype == NCZ_DTYPE_F16;
-    const size_t vec_elems = p.o_f16 ? 8 : 4;
+    p.o_dtype = r.o_dtype == NCZ_DTYPE_F16 ? 1 : (r.o_dtype == NCZ_DTYPE_BF16 ? 2 : 0);
+    const size_t vec_elems = p.o_dtype != 0 ? 8 : 4;
     p.o_vec = aligned(r.o, 16) && r.os % vec_elems == 0 && r.orow % vec_elems == 0;
     choose_splits(r, dev, &p.num_splits, &p.kv_per_split);
     if (r.scratch != nullptr) {
@@ -323,20 +345,12 @@ int launch_on_current(const Resolved &r, int dev) {
     }
     const unsigned grid =
         static_cast<unsigned>(static_cast<size_t>(p.num_groups) * r.bh * static_cast<size_t>(p.num_splits));
+    const bool bf = r.in_dtype == NCZ_DTYPE_BF16;
     int st;
     switch (r.d) {
-        case 16: st = use_tma ? launch_variant<16, true>(tq, tk, tv, p, grid, dev, r.stream)
-                              : launch_variant<16, false>(tq, tk, tv, p, grid, dev, r.stream);
-            if (st == NCZ_SUCCESS && p.num_splits > 1) st = launch_combine<16>(p, r.stream);
-            break;
-        case 32: st = use_tma ? launch_variant<32, true>(tq, tk, tv, p, grid, dev, r.stream)
-                              : launch_variant<32, false>(tq, tk, tv, p, grid, dev, r.stream);
-            if (st == NCZ_SUCCESS && p.num_splits > 1) st = launch_combine<32>(p, r.stream);
-            break;
-        default: st = use_tma ? launch_variant<64, true>(tq, tk, tv, p, grid, dev, r.stream)
-                              : launch_variant<64, false>(tq, tk, tv, p, grid, dev, r.stream);
-            if (st == NCZ_SUCCESS && p.num_splits > 1) st = launch_combine<64>(p, r.stream);
-            break;
+        case 16: st = launch_d<16>(use_tma, bf, tq, tk, tv, p, grid, dev, r.stream); break;
+        case 32: st = launch_d<32>(use_tma, bf, tq, tk, tv, p, grid, dev, r.stream); break;
+        default: st = launch_d<64>(use_tma, bf, tq, tk, tv, p, grid, dev, r.stream); break;
     }
     if (ws != nullptr) {
         const cudaError_t e = cudaFreeAsync(ws, r.stream);
@@ -380,6 +394,7 @@ Resolved reference_args(const void *q, const void *k, const void *v, void *o, si
     desc.q_stride = qs; desc.k_stride = ks; desc.v_stride = vs; desc.o_stride = os;
     desc.scale = scale; desc.causal = causal;
     desc.o_dtype = NCZ_DTYPE_F32; desc.producer = NCZ_PRODUCER_AUTO; desc.device = -1;
+    desc.in_dtype = NCZ_DTYPE_F16;
     desc.stream = stream;
     return from_desc(desc);
 }
@@ -441,7 +456,7 @@ int host_pipeline(const Resolved &r, const void *qh, const void *kh, const void 
     std::lock_guard<std::mutex> lock(hp.mu);
     int st = pipe_setup(hp);
     if (st != NCZ_SUCCESS) return st;
-    const size_t osz = r.o_dtype == NCZ_DTYPE_F16 ? 2 : 4;
+    const size_t osz = r.o_dtype == NCZ_DTYPE_F32 ? 4 : 2;
     cudaError_t e = cudaEventRecord(hp.fork, r.stream);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(hp.up, hp.fork, 0);
     if (e == cudaSuccess) e = cudaStreamWaitEvent(hp.down, hp.fork, 0);
@@ -728,6 +743,10 @@ uint64_t ncz_launch_count(void) { return g_launches.load(std::memory_order_relax
 
 uint64_t ncz_umma_smem_desc(uint32_t smem_addr, uint32_t lbo_bytes, uint32_t sbo_bytes, uint32_t layout_type) {
     return ncz::umma_smem_desc(smem_addr, lbo_bytes, sbo_bytes, layout_type);
+}
+
+uint32_t ncz_umma_instr_desc_bf16(uint32_t m, uint32_t n, uint32_t a_major, uint32_t b_major) {
+    return ncz::umma_idesc_f16_f32(m, n, a_major, b_major, 1u);
 }
 
 uint32_t ncz_umma_instr_desc_f16(uint32_t m, uint32_t n, uint32_t a_major, uint32_t b_major) {

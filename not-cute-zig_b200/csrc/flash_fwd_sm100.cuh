@@ -36,6 +36,7 @@
 // all roles leave their loops; issued copies and MMAs are waited for
 // (bounded) before TMEM is freed and the CTA exits.  No trap, no assert.
 #pragma once
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cstdint>
 
@@ -101,7 +102,7 @@ struct FlashParams {
     int num_groups;    // ceil(seq_len / 256)
     float scale_log2;  // scale * log2(e)
     int causal;
-    int o_f16;
+    int o_dtype;  // 0 f32, 1 f16, 2 bf16
     int o_vec;  // 16-byte vector stores of O are aligned
     // Split-KV: num_splits > 1 splits each Q group's K tiles into ranges of
     // kv_per_split tiles, one CTA per range; CTAs then write unnormalised partial
@@ -217,31 +218,6 @@ __device__ __forceinline__ bool bounded_wait(uint32_t bar, uint32_t parity, vola
                                              uint32_t site, bool honor_abort) {
     if (mbar_try_wait(bar, parity)) return true;
     return bounded_wait_slow(bar, parity, abort_flag, site, honor_abort);
-}
-
-// Same wait with the slow loop inlined: for waits taken while many registers
-// are live, where an out-of-line call would make the caller spill them.
-__device__ __forceinline__ bool warp_wait_inline(uint32_t bar, uint32_t parity, volatile uint32_t *abort_flag,
-                                                 uint32_t site) {
-    bool ok = mbar_try_wait(bar, parity);
-    if (!ok) {
-        const unsigned long long t0 = sm_clock();
-        for (uint32_t it = 1;; ++it) {
-            if (mbar_try_wait(bar, parity)) {
-                ok = true;
-                break;
-            }
-            if ((it & 15u) == 0u) {
-                if (*abort_flag) break;
-                if (sm_clock() - t0 > g_ncz_wait_limit) {
-                    *abort_flag = 1u;
-                    atomicCAS(&g_ncz_status, 0u, 0x80000000u | (site << 24) | (blockIdx.x & 0xFFFFFFu));
-                    break;
-                }
-            }
-        }
-    }
-    return __all_sync(0xffffffffu, ok);
 }
 
 // All lanes wait; the result is made warp-uniform so .sync.aligned tcgen05
@@ -384,20 +360,20 @@ __device__ __forceinline__ void producer_lsu(const FlashParams &p, uint8_t *smem
 // ---------------------------------------------------------------------------
 // MMA issuer (whole warp; elect.sync picks the issuing lane)
 // ---------------------------------------------------------------------------
-template <int D>
+template <int D, bool kBf16>
 __device__ __forceinline__ void issue_qk(int j, uint32_t sbase, uint32_t tS, uint64_t qdesc) {
     using L = SmemLayout<D>;
-    constexpr uint32_t idesc_qk = umma_idesc_f16_f32(kBlockM, kBlockN, 0, 0);  // both K-major
+    constexpr uint32_t idesc_qk = umma_idesc_f16_f32(kBlockM, kBlockN, 0, 0, kBf16);  // both K-major
     const int st = j % L::kStages;
     const uint64_t kdesc = umma_smem_desc(sbase + L::kOffK + st * L::kKvTile, 16, 8 * L::kSpan, L::kUmmaLayout);
     // K advance: 32 bytes (2 encoded units) inside the swizzled row per step
     umma_ss_chain_elect<D / 16>(tS, qdesc, kdesc, idesc_qk);
 }
 
-template <int D>
+template <int D, bool kBf16>
 __device__ __forceinline__ void issue_pv(int j, uint32_t sbase, uint32_t tP, uint32_t tO) {
     using L = SmemLayout<D>;
-    constexpr uint32_t idesc_pv = umma_idesc_f16_f32(kBlockM, D, 0, 1);  // B = V, MN-major
+    constexpr uint32_t idesc_pv = umma_idesc_f16_f32(kBlockM, D, 0, 1, kBf16);  // B = V, MN-major
     const int st = j % L::kStages;
     // V tile: kBlockN keys x D, rows of 2D bytes (one swizzle atom wide); 8-row groups 8*span apart.
     const uint64_t vdesc =
@@ -412,7 +388,7 @@ __device__ __forceinline__ void issue_pv(int j, uint32_t sbase, uint32_t tP, uin
 // P_w(j) is stored and V(j) is resident.  Each warp arrives once per K tile on
 // the stage's kv_empty barrier (a commit after its PV, or a plain arrive past
 // its causal range), so a stage is released when both Q tiles are done with it.
-template <int D>
+template <int D, bool kBf16>
 __device__ __forceinline__ void mma_role(int w, uint32_t sbase, uint32_t tmem, const Work &wk,
                                          volatile uint32_t *abort_flag, int lane) {
     using L = SmemLayout<D>;
@@ -425,7 +401,7 @@ __device__ __forceinline__ void mma_role(int w, uint32_t sbase, uint32_t tmem, c
         ok = warp_wait(b.q_full(), 0, abort_flag, kSiteQFull) && warp_wait(b.k_full(0), 0, abort_flag, kSiteKFull);
         if (ok) {
             tc_fence_after();
-            issue_qk<D>(0, sbase, tS, qdesc);
+            issue_qk<D, kBf16>(0, sbase, tS, qdesc);
             if (!(w == 0 && g_ncz_test_drop != 0)) umma_commit_elect(b.s_full(w));
         }
     }
@@ -438,14 +414,14 @@ __device__ __forceinline__ void mma_role(int w, uint32_t sbase, uint32_t tmem, c
                  warp_wait(b.k_full(st1), ((j + 1) / L::kStages) & 1, abort_flag, kSiteKFull);
             if (!ok) break;
             tc_fence_after();
-            issue_qk<D>(j + 1, sbase, tS, qdesc);
+            issue_qk<D, kBf16>(j + 1, sbase, tS, qdesc);
             umma_commit_elect(b.s_full(w));
         }
         ok = warp_wait(b.v_full(st), (j / L::kStages) & 1, abort_flag, kSiteVFull) &&
              warp_wait(b.p_full(w), j & 1, abort_flag, kSitePFull);
         if (!ok) break;
         tc_fence_after();
-        issue_pv<D>(j, sbase, tP, tO);
+        issue_pv<D, kBf16>(j, sbase, tP, tO);
         umma_commit_elect(b.o_done(w));
         umma_commit_elect(b.kv_empty(st));  // this Q tile is done with K(j) and V(j)
     }
@@ -508,24 +484,27 @@ template <int N>
 __device__ __forceinline__ void write_o_global(const FlashParams &p, const Work &wk, int row, const float (&o)[N],
                                                float l) {
     const float inv = 1.0f / l;
-    if (p.o_f16) {
-        __half *orow = reinterpret_cast<__half *>(p.o) + wk.slice * p.o_stride + static_cast<long long>(row) * p.o_row;
+    const long long base = wk.slice * p.o_stride + static_cast<long long>(row) * p.o_row;
+    if (p.o_dtype != 0) {  // 16-bit O: f16 (1) or bf16 (2)
+        uint16_t *orow = reinterpret_cast<uint16_t *>(p.o) + base;
+        const bool bf = p.o_dtype == 2;
         if (p.o_vec) {
 #pragma unroll
             for (int c = 0; c < N; c += 8) {
                 uint4 v;
-                v.x = pack_f16x2(o[c + 0] * inv, o[c + 1] * inv);
-                v.y = pack_f16x2(o[c + 2] * inv, o[c + 3] * inv);
-                v.z = pack_f16x2(o[c + 4] * inv, o[c + 5] * inv);
-                v.w = pack_f16x2(o[c + 6] * inv, o[c + 7] * inv);
+                v.x = bf ? pack_bf16x2(o[c + 0] * inv, o[c + 1] * inv) : pack_f16x2(o[c + 0] * inv, o[c + 1] * inv);
+                v.y = bf ? pack_bf16x2(o[c + 2] * inv, o[c + 3] * inv) : pack_f16x2(o[c + 2] * inv, o[c + 3] * inv);
+                v.z = bf ? pack_bf16x2(o[c + 4] * inv, o[c + 5] * inv) : pack_f16x2(o[c + 4] * inv, o[c + 5] * inv);
+                v.w = bf ? pack_bf16x2(o[c + 6] * inv, o[c + 7] * inv) : pack_f16x2(o[c + 6] * inv, o[c + 7] * inv);
                 *reinterpret_cast<uint4 *>(orow + c) = v;
             }
         } else {
 #pragma unroll
-            for (int c = 0; c < N; ++c) orow[c] = __float2half_rn(o[c] * inv);
+            for (int c = 0; c < N; ++c)
+                orow[c] = static_cast<uint16_t>(bf ? pack_bf16x2(o[c] * inv, 0.0f) : pack_f16x2(o[c] * inv, 0.0f));
         }
     } else {
-        float *orow = reinterpret_cast<float *>(p.o) + wk.slice * p.o_stride + static_cast<long long>(row) * p.o_row;
+        float *orow = reinterpret_cast<float *>(p.o) + base;
         if (p.o_vec) {
 #pragma unroll
             for (int c = 0; c < N; c += 4)
@@ -563,8 +542,10 @@ __device__ __forceinline__ float row_max(const float (&x)[kBlockN]) {
 }
 
 // Exponentiates one score row in place against base m (log2 domain), packs P
-// to f16 pairs (rounded as src/flash_h64_bn32.zig:185) and sums the unrounded
-// values in four independent chains.
+// to pairs of the input type (f16 as src/flash_h64_bn32.zig:185, or bf16: the
+// PV MMA takes A and B of one type) and sums the unrounded values in four
+// independent chains.
+template <bool kBf16>
 __device__ __forceinline__ float exp_row(float (&x)[kBlockN], float kmul, float m, uint32_t (&pk)[kBlockN / 2]) {
     const uint64_t kmul2 = pack_f32x2(kmul, kmul), negm2 = pack_f32x2(-m, -m);
     uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};  // (0.0f, 0.0f) x 4
@@ -579,7 +560,7 @@ __device__ __forceinline__ float exp_row(float (&x)[kBlockN], float kmul, float 
             p1 = ex2_approx(e1);
         }
         sum2[c & 3] = fadd2(sum2[c & 3], pack_f32x2(p0, p1));
-        pk[c] = pack_f16x2(p0, p1);
+        pk[c] = pack_in_x2<kBf16>(p0, p1);
     }
     float s0, s1;
     unpack_f32x2(fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3])), s0, s1);
@@ -611,31 +592,7 @@ __device__ __forceinline__ void prep_scores(float (&x)[kBlockN], bool pre_scale,
     }
 }
 
-// Exponentiates keys c0 .. c0+31 against base m (log2 domain), packs P to f16
-// pairs (rounded as src/flash_h64_bn32.zig:185) and sums the unrounded values.
-__device__ __forceinline__ float exp_chunk(const float (&x)[kBlockN], int c0, float kmul, float m,
-                                           uint32_t (&pk)[16]) {
-    const uint64_t kmul2 = pack_f32x2(kmul, kmul), negm2 = pack_f32x2(-m, -m);
-    uint64_t sum2[2] = {0ull, 0ull};  // (0.0f, 0.0f) x 2
-#pragma unroll
-    for (int c = 0; c < 16; ++c) {
-        float e0, e1, p0, p1;
-        unpack_f32x2(ffma2(pack_f32x2(x[c0 + 2 * c], x[c0 + 2 * c + 1]), kmul2, negm2), e0, e1);
-        if (kExp2EmuPeriod > 0 && c % kExp2EmuPeriod >= kExp2EmuPeriod - kExp2EmuCount) {
-            exp2_poly_x2(e0, e1, p0, p1);  // FMA pipe
-        } else {
-            p0 = ex2_approx(e0);  // MUFU
-            p1 = ex2_approx(e1);
-        }
-        sum2[c & 1] = fadd2(sum2[c & 1], pack_f32x2(p0, p1));
-        pk[c] = pack_f16x2(p0, p1);
-    }
-    float s0, s1;
-    unpack_f32x2(fadd2(sum2[0], sum2[1]), s0, s1);
-    return s0 + s1;
-}
-
-template <int D>
+template <int D, bool kBf16>
 __device__ __forceinline__ void softmax_role(const FlashParams &p, uint32_t sbase, uint32_t tmem, const Work &wk,
                                              volatile uint32_t *abort_flag, int warp, int lane) {
     const Bars<D> b{sbase};
@@ -694,7 +651,7 @@ __device__ __forceinline__ void softmax_role(const FlashParams &p, uint32_t sbas
             if (!ok) break;
         }
         uint32_t pk[kBlockN / 2];
-        const float tsum = exp_row(x, kmul, m_use, pk);
+        const float tsum = exp_row<kBf16>(x, kmul, m_use, pk);
         if (kExpTurns && (w == 0 ? (j < n_other) : (j + 1 < n_other))) {
             __syncwarp();
             if (lane == 0) mbar_arrive(b.turn(sub, w ^ 1));
@@ -743,7 +700,7 @@ __device__ __forceinline__ void softmax_role(const FlashParams &p, uint32_t sbas
 // ---------------------------------------------------------------------------
 // kernel
 // ---------------------------------------------------------------------------
-template <int D, bool kTma>
+template <int D, bool kTma, bool kBf16>
 __global__ void __launch_bounds__(kThreads, 1)
     flash_fwd_sm100(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                     const __grid_constant__ CUtensorMap tmap_v, const __grid_constant__ FlashParams p) {
@@ -802,9 +759,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
     } else if (warp == 1 || warp == 2) {
-        mma_role<D>(warp - 1, sbase, tmem, wk, abort_flag, lane);
+        mma_role<D, kBf16>(warp - 1, sbase, tmem, wk, abort_flag, lane);
     } else if (warp >= 4) {
-        softmax_role<D>(p, sbase, tmem, wk, abort_flag, warp, lane);
+        softmax_role<D, kBf16>(p, sbase, tmem, wk, abort_flag, warp, lane);
     }
 
     tc_fence_before();
@@ -867,8 +824,10 @@ __global__ void __launch_bounds__(256) combine_splits(const __grid_constant__ Fl
     const long long base = slice * p.o_stride + static_cast<long long>(row) * p.o_row + lane * kPer;
 #pragma unroll
     for (int c = 0; c < kPer; ++c) {
-        if (p.o_f16) {
+        if (p.o_dtype == 1) {
             reinterpret_cast<__half *>(p.o)[base + c] = __float2half_rn(acc[c] * inv);
+        } else if (p.o_dtype == 2) {
+            reinterpret_cast<__nv_bfloat16 *>(p.o)[base + c] = __float2bfloat16_rn(acc[c] * inv);
         } else {
             reinterpret_cast<float *>(p.o)[base + c] = acc[c] * inv;
         }

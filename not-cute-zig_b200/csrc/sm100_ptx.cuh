@@ -29,9 +29,9 @@ __host__ __device__ constexpr uint64_t umma_smem_desc(uint32_t smem_addr, uint32
 }
 
 __host__ __device__ constexpr uint32_t umma_idesc_f16_f32(uint32_t m, uint32_t n, uint32_t a_mn_major,
-                                                          uint32_t b_mn_major) {
-    return (1u << 4)                  // D = f32
-           | (0u << 7) | (0u << 10)   // A, B = f16
+                                                          uint32_t b_mn_major, uint32_t bf16 = 0) {
+    return (1u << 4)                                     // D = f32
+           | ((bf16 & 1u) << 7) | ((bf16 & 1u) << 10)    // A, B = f16 (0) or bf16 (1), always alike
            | ((a_mn_major & 1u) << 15) | ((b_mn_major & 1u) << 16) |
            (((n >> 3) & 0x3Fu) << 17) | (((m >> 4) & 0x1Fu) << 24);
 }
@@ -477,6 +477,22 @@ __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
     uint32_t r;
     asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
     return r;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+// 16-bit pair of the input type: f16 or bf16, round to nearest even.
+template <bool kBf16>
+__device__ __forceinline__ uint32_t pack_in_x2(float lo, float hi) {
+    if constexpr (kBf16) {
+        return pack_bf16x2(lo, hi);
+    } else {
+        return pack_f16x2(lo, hi);
+    }
 }
 
 }  // namespace ncz

@@ -47,7 +47,7 @@ STATUS_NAMES = {
     18: "Misaligned",
 }
 
-DTYPE_F32, DTYPE_F16 = 0, 1
+DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 PRODUCERS = {"auto": 0, "tma": 1, "lsu": 2}
 
 
@@ -83,6 +83,7 @@ class _Desc(ctypes.Structure):
         ("producer", ctypes.c_int32),
         ("device", ctypes.c_int32),
         ("stream", ctypes.c_void_p),
+        ("in_dtype", ctypes.c_int32),
     ]
 
 
@@ -117,6 +118,7 @@ _SIGNATURES = {
     "ncz_launch_count": (ctypes.c_uint64, []),
     "ncz_umma_smem_desc": (ctypes.c_uint64, [ctypes.c_uint32] * 4),
     "ncz_umma_instr_desc_f16": (ctypes.c_uint32, [ctypes.c_uint32] * 4),
+    "ncz_umma_instr_desc_bf16": (ctypes.c_uint32, [ctypes.c_uint32] * 4),
     "ncz_tma_swizzle_offset": (ctypes.c_uint32, [ctypes.c_uint32] * 2),
 }
 
@@ -241,15 +243,20 @@ def launch(q, k, v, o, opts: Options, stream=None) -> None:
 def make_desc(q, k, v, o, opts: Options, *, row_strides: Optional[Sequence[int]] = None,
               producer: str = "auto", device: Optional[int] = None, stream=None) -> _Desc:
     """Extended descriptor (ncz_flash_desc): row strides (default head_dim),
-    O float32 or float16 (taken from o.dtype), producer override, device."""
+    Q/K/V float16 or bfloat16 and O float32, float16 or bfloat16 (taken from
+    the tensors' dtypes), producer override, device."""
     import torch
 
-    _require(q, "float16", "q")
-    _require(k, "float16", "k")
-    _require(v, "float16", "v")
-    if o.dtype not in (torch.float32, torch.float16):
-        raise FlashError(5, "o must be float32 or float16")
-    _require(o, "float32" if o.dtype == torch.float32 else "float16", "o")
+    if q.dtype not in (torch.float16, torch.bfloat16):
+        raise FlashError(5, "q must be float16 or bfloat16")
+    in_name = "float16" if q.dtype == torch.float16 else "bfloat16"
+    _require(q, in_name, "q")
+    _require(k, in_name, "k")
+    _require(v, in_name, "v")
+    o_types = {torch.float32: DTYPE_F32, torch.float16: DTYPE_F16, torch.bfloat16: DTYPE_BF16}
+    if o.dtype not in o_types:
+        raise FlashError(5, "o must be float32, float16 or bfloat16")
+    _require(o, str(o.dtype).replace("torch.", ""), "o")
     rs = list(row_strides) if row_strides is not None else [0, 0, 0, 0]
     d = _Desc()
     d.q, d.k, d.v, d.o = q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr()
@@ -258,7 +265,8 @@ def make_desc(q, k, v, o, opts: Options, *, row_strides: Optional[Sequence[int]]
     d.q_row_stride, d.k_row_stride, d.v_row_stride, d.o_row_stride = rs
     d.scale = float(opts.scale)
     d.causal = int(bool(opts.causal))
-    d.o_dtype = DTYPE_F32 if o.dtype == torch.float32 else DTYPE_F16
+    d.o_dtype = o_types[o.dtype]
+    d.in_dtype = DTYPE_F16 if q.dtype == torch.float16 else DTYPE_BF16
     d.producer = PRODUCERS[producer]
     d.device = q.device.index if device is None else device
     d.stream = _stream_handle(stream)

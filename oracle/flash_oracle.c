@@ -41,6 +41,23 @@ static inline float h2f(f16bits h) {
     return (float)v;
 }
 
+/* bf16 bits -> f32: the upper half of the f32 bit pattern (exact). */
+static inline float b2f(f16bits h) {
+    uint32_t u = (uint32_t)h << 16;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+/* f32 -> bf16 bits, round to nearest even (NaN kept quiet). */
+static inline f16bits f2b(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    if ((u & 0x7F800000u) == 0x7F800000u && (u & 0x007FFFFFu) != 0u) return (f16bits)((u >> 16) | 0x40u);
+    u += 0x7FFFu + ((u >> 16) & 1u);
+    return (f16bits)(u >> 16);
+}
+
 static inline f16bits f2h(float f) {
     _Float16 v = (_Float16)f; /* round to nearest even */
     f16bits h;
@@ -53,7 +70,8 @@ static inline f16bits f2h(float f) {
 static void flash_one_row(size_t seq_len, size_t head_dim, size_t row, const f16bits *q,
                           size_t q_row, const f16bits *k, size_t k_row, const f16bits *v,
                           size_t v_row, float *o, size_t o_row, float scale, uint32_t causal,
-                          float *scores) {
+                          float *scores, int bf16) {
+    float (*const in)(f16bits) = bf16 ? b2f : h2f; /* Q/K/V element type */
     float row_max = -INFINITY;
     for (size_t key = 0; key < seq_len; ++key) {
         if (causal != 0 && key > row) {
@@ -61,7 +79,7 @@ static void flash_one_row(size_t seq_len, size_t head_dim, size_t row, const f16
         } else {
             float score = 0.0f;
             for (size_t kk = 0; kk < head_dim; ++kk) /* main.zig:1281-1284 */
-                score += h2f(q[row * q_row + kk]) * h2f(k[key * k_row + kk]);
+                score += in(q[row * q_row + kk]) * in(k[key * k_row + kk]);
             score *= scale; /* main.zig:1285 */
             scores[key] = score;
             row_max = fmaxf(row_max, score);
@@ -77,7 +95,7 @@ static void flash_one_row(size_t seq_len, size_t head_dim, size_t row, const f16
         float acc = 0.0f;
         for (size_t key = 0; key < seq_len; ++key) {
             const float weight = scores[key] / row_sum;
-            acc += weight * h2f(v[key * v_row + col]);
+            acc += weight * in(v[key * v_row + col]);
         }
         o[row * o_row + col] = acc;
     }
@@ -91,11 +109,11 @@ static void flash_one_row(size_t seq_len, size_t head_dim, size_t row, const f16
  * 0..seq_len); the CPU baseline uses a subrange as its bounded sample.
  * Output elements outside the active rows are not touched.
  */
-void ncz_oracle_flash(size_t batch_heads, size_t seq_len, size_t head_dim, const f16bits *q,
-                      size_t q_stride, size_t q_row, const f16bits *k, size_t k_stride,
-                      size_t k_row, const f16bits *v, size_t v_stride, size_t v_row, float *o,
-                      size_t o_stride, size_t o_row, float scale, uint32_t causal,
-                      size_t row_begin, size_t row_end, int nthreads) {
+static void oracle_flash(size_t batch_heads, size_t seq_len, size_t head_dim, const f16bits *q,
+                         size_t q_stride, size_t q_row, const f16bits *k, size_t k_stride,
+                         size_t k_row, const f16bits *v, size_t v_stride, size_t v_row, float *o,
+                         size_t o_stride, size_t o_row, float scale, uint32_t causal,
+                         size_t row_begin, size_t row_end, int nthreads, int bf16) {
     if (row_end > seq_len) row_end = seq_len;
     if (row_begin >= row_end || batch_heads == 0) return;
     const size_t rows = row_end - row_begin;
@@ -114,10 +132,30 @@ void ncz_oracle_flash(size_t batch_heads, size_t seq_len, size_t head_dim, const
             const size_t row = row_begin + (size_t)i % rows;
             flash_one_row(seq_len, head_dim, row, q + slice * q_stride, q_row,
                           k + slice * k_stride, k_row, v + slice * v_stride, v_row,
-                          o + slice * o_stride, o_row, scale, causal, scores);
+                          o + slice * o_stride, o_row, scale, causal, scores, bf16);
         }
         free(scores);
     }
+}
+
+void ncz_oracle_flash(size_t batch_heads, size_t seq_len, size_t head_dim, const f16bits *q,
+                      size_t q_stride, size_t q_row, const f16bits *k, size_t k_stride,
+                      size_t k_row, const f16bits *v, size_t v_stride, size_t v_row, float *o,
+                      size_t o_stride, size_t o_row, float scale, uint32_t causal,
+                      size_t row_begin, size_t row_end, int nthreads) {
+    oracle_flash(batch_heads, seq_len, head_dim, q, q_stride, q_row, k, k_stride, k_row, v, v_stride,
+                 v_row, o, o_stride, o_row, scale, causal, row_begin, row_end, nthreads, 0);
+}
+
+/* The same maths on bf16 Q/K/V (the reference has f16 only; this extends the
+ * restatement to the bf16 input path of the kernel). */
+void ncz_oracle_flash_bf16(size_t batch_heads, size_t seq_len, size_t head_dim, const f16bits *q,
+                           size_t q_stride, size_t q_row, const f16bits *k, size_t k_stride,
+                           size_t k_row, const f16bits *v, size_t v_stride, size_t v_row, float *o,
+                           size_t o_stride, size_t o_row, float scale, uint32_t causal,
+                           size_t row_begin, size_t row_end, int nthreads) {
+    oracle_flash(batch_heads, seq_len, head_dim, q, q_stride, q_row, k, k_stride, k_row, v, v_stride,
+                 v_row, o, o_stride, o_row, scale, causal, row_begin, row_end, nthreads, 1);
 }
 
 /* fillFlashInput (src/main.zig:1207-1211):
@@ -142,18 +180,27 @@ static inline double uniform01(uint64_t *state) {
 }
 
 /* f16(mean + std * N(0,1)); Box-Muller on pairs from splitmix64(seed). */
-void ncz_oracle_fill_normal(f16bits *data, size_t n, uint64_t seed, float mean, float stddev) {
+static void fill_normal_as(f16bits *data, size_t n, uint64_t seed, float mean, float stddev,
+                           f16bits (*enc)(float)) {
     uint64_t state = seed;
     const double two_pi = 6.283185307179586476925286766559;
     for (size_t i = 0; i < n; i += 2) {
         const double u1 = uniform01(&state), u2 = uniform01(&state);
         const double r = sqrt(-2.0 * log(u1));
-        data[i] = f2h((float)(mean + stddev * r * cos(two_pi * u2)));
-        if (i + 1 < n) data[i + 1] = f2h((float)(mean + stddev * r * sin(two_pi * u2)));
+        data[i] = enc((float)(mean + stddev * r * cos(two_pi * u2)));
+        if (i + 1 < n) data[i + 1] = enc((float)(mean + stddev * r * sin(two_pi * u2)));
     }
 }
 
-/* f16(U(lo, hi)) from splitmix64(seed). */
+void ncz_oracle_fill_normal(f16bits *data, size_t n, uint64_t seed, float mean, float stddev) {
+    fill_normal_as(data, n, seed, mean, stddev, f2h);
+}
+
+/* bf16 (round to nearest even) from the same splitmix64 + Box-Muller stream. */
+void ncz_oracle_fill_normal_bf16(f16bits *data, size_t n, uint64_t seed, float mean, float stddev) {
+    fill_normal_as(data, n, seed, mean, stddev, f2b);
+}
+
 void ncz_oracle_fill_uniform(f16bits *data, size_t n, uint64_t seed, float lo, float hi) {
     uint64_t state = seed;
     for (size_t i = 0; i < n; ++i) data[i] = f2h((float)(lo + (hi - lo) * uniform01(&state)));

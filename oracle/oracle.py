@@ -20,13 +20,19 @@ _lib = None
 def lib() -> ctypes.CDLL:
     global _lib
     if _lib is None:
-        if not os.path.exists(_build.ORACLE_SO):
+        src = os.path.join(os.path.dirname(os.path.abspath(__file__)), "flash_oracle.c")
+        if not os.path.exists(_build.ORACLE_SO) or (
+                os.path.exists(src) and os.path.getmtime(src) > os.path.getmtime(_build.ORACLE_SO)):
             _build.build_oracle()
         h = ctypes.CDLL(_build.ORACLE_SO)
         sz, vp = ctypes.c_size_t, ctypes.c_void_p
         h.ncz_oracle_flash.restype = None
         h.ncz_oracle_flash.argtypes = [sz, sz, sz, vp, sz, sz, vp, sz, sz, vp, sz, sz, vp, sz, sz,
                                        ctypes.c_float, ctypes.c_uint32, sz, sz, ctypes.c_int]
+        h.ncz_oracle_flash_bf16.restype = None
+        h.ncz_oracle_flash_bf16.argtypes = h.ncz_oracle_flash.argtypes
+        h.ncz_oracle_fill_normal_bf16.restype = None
+        h.ncz_oracle_fill_normal_bf16.argtypes = [vp, sz, ctypes.c_uint64, ctypes.c_float, ctypes.c_float]
         h.ncz_oracle_fill_pattern.restype = None
         h.ncz_oracle_fill_pattern.argtypes = [vp, sz, sz, sz, sz, ctypes.c_float]
         h.ncz_oracle_fill_normal.restype = None
@@ -84,15 +90,28 @@ def flash_reference(q: np.ndarray, k: np.ndarray, v: np.ndarray, *, batch_heads:
     Returns a float32 array of batch_heads * o_stride elements (unwritten
     elements are 0, as the reference's `expected` buffer is zero-filled)."""
     qr, kr, vr, orow = row_strides if row_strides is not None else (head_dim,) * 4
+    bf16 = q.dtype == np.uint16  # bf16 bit patterns (numpy has no bf16 type)
     for a in (q, k, v):
-        assert a.dtype == np.float16 and a.flags.c_contiguous
+        assert a.dtype == (np.uint16 if bf16 else np.float16) and a.flags.c_contiguous
     if out is None:
         out = np.zeros(batch_heads * o_stride, dtype=np.float32)
     r0, r1 = rows if rows is not None else (0, seq_len)
-    lib().ncz_oracle_flash(batch_heads, seq_len, head_dim, _ptr(q), q_stride, qr, _ptr(k), k_stride, kr,
-                           _ptr(v), v_stride, vr, _ptr(out), o_stride, orow, float(scale), int(bool(causal)),
-                           r0, r1, threads)
+    fn = lib().ncz_oracle_flash_bf16 if bf16 else lib().ncz_oracle_flash
+    fn(batch_heads, seq_len, head_dim, _ptr(q), q_stride, qr, _ptr(k), k_stride, kr,
+       _ptr(v), v_stride, vr, _ptr(out), o_stride, orow, float(scale), int(bool(causal)), r0, r1, threads)
     return out
+
+
+def fill_normal_bf16(n: int, seed: int, mean: float = 0.0, std: float = 1.0) -> np.ndarray:
+    """bf16(mean + std * N(0,1)) bit patterns (uint16) from splitmix64(seed) + Box-Muller,
+    the same stream as fill_normal."""
+    out = np.empty(n, dtype=np.uint16)
+    lib().ncz_oracle_fill_normal_bf16(_ptr(out), n, seed, mean, std)
+    return out
+
+
+def bf16_to_f32(bits: np.ndarray) -> np.ndarray:
+    return (bits.astype(np.uint32) << 16).view(np.float32)
 
 
 def max_threads() -> int:

@@ -19,6 +19,11 @@ import numpy as np
 
 ATOL = 2e-3
 NORM_RTOL = 1e-2
+# bf16 inputs (an extension: the reference is f16 only).  The kernel rounds P
+# to bf16 before PV (a tensor-core MMA takes A and B of one type), 3 mantissa
+# bits fewer than f16, so the bound is 4x the f16 one; the oracle reads the same
+# bf16 Q/K/V bits and does not round P.
+ATOL_BF16 = 8e-3
 
 # The reference smoke cases, src/main.zig:190-193:
 # (batch_heads, seq_len, head_dim, q/k/v/o slice strides, causal)
@@ -78,6 +83,16 @@ def normal_problem(bh, seq, d, causal, seed, oracle, std=0.5, k_mul=1.0, strides
     return p
 
 
+def normal_problem_bf16(bh, seq, d, causal, seed, oracle, std=0.5, k_mul=1.0, strides=None, scale=None):
+    """normal_problem with bf16 Q/K/V (uint16 bit patterns, same random stream)."""
+    st = strides or (seq * d,) * 4
+    p = Problem(bh, seq, d, st, causal, scale if scale is not None else 1.0 / math.sqrt(d))
+    p.q = oracle.fill_normal_bf16(bh * st[0], seed * 3 + 0, 0.0, std)
+    p.k = oracle.fill_normal_bf16(bh * st[1], seed * 3 + 1, 0.0, std * k_mul)
+    p.v = oracle.fill_normal_bf16(bh * st[2], seed * 3 + 2, 0.0, std)
+    return p
+
+
 def reference(p: Problem, oracle, slices=None, rows=None):
     """Oracle output (float32, bh * o_stride elements, zeros outside the active region).
 
@@ -117,11 +132,11 @@ def compare(got: np.ndarray, want: np.ndarray, idx: np.ndarray):
     return max_abs, norm_rel
 
 
-def check(got, want, idx, what=""):
+def check(got, want, idx, what="", atol=ATOL, rtol=NORM_RTOL):
     max_abs, norm_rel = compare(got, want, idx)
     log = os.environ.get("NCZ_PARITY_LOG")
     if log:
         with open(log, "a") as f:
             f.write(f"{what}\tmax_abs={max_abs:.3e}\tnorm_rel={norm_rel:.3e}\telements={idx.size}\n")
-    assert max_abs <= ATOL and norm_rel <= NORM_RTOL, f"{what}: max_abs={max_abs:.3e} norm_rel={norm_rel:.3e}"
+    assert max_abs <= atol and norm_rel <= rtol, f"{what}: max_abs={max_abs:.3e} norm_rel={norm_rel:.3e}"
     return max_abs, norm_rel

@@ -244,3 +244,20 @@ def test_split_entry_points_validate(ncz):
         bad = D.from_buffer_copy(good)
         bad.seq_len = 0
         assert ncz.flash.STATUS_NAMES[fn(ctypes.byref(bad), 2)] == "InvalidValue"
+
+
+def test_umma_instr_descriptor_bf16(ncz):
+    lib = ncz.flash.lib()
+    assert lib.ncz_umma_instr_desc_bf16(128, 128, 0, 0) == lib.ncz_umma_instr_desc_f16(128, 128, 0, 0) | (1 << 7) | (1 << 10)
+    assert lib.ncz_umma_instr_desc_bf16(128, 64, 0, 1) == lib.ncz_umma_instr_desc_f16(128, 64, 0, 1) | (1 << 7) | (1 << 10)
+
+
+def test_validate_ex_dtypes(ncz):
+    lib = ncz.flash.lib()
+    D = ncz.flash._Desc
+    st = 64 * 16
+    for in_dt, o_dt, ok in ((0, 0, True), (1, 1, True), (2, 2, True), (2, 0, True), (1, 2, True),
+                            (3, 0, False), (2, 3, False), (-1, 0, False)):
+        d = D(q=1, k=1, v=1, o=1, batch_heads=2, seq_len=64, head_dim=16, q_stride=st, k_stride=st, v_stride=st,
+              o_stride=st, scale=0.25, causal=1, o_dtype=o_dt, producer=0, device=-1, stream=None, in_dtype=in_dt)
+        assert (lib.ncz_flash_validate_ex(ctypes.byref(d)) == 0) == ok, (in_dt, o_dt)

@@ -455,3 +455,54 @@ def test_host_pipeline_tapered_default_matches_device_launch(ncz, oracle_mod):
     assert ncz.flash.launch_count() - before == 11
     assert ncz.sync_status() == 0
     assert torch.equal(oh, o_ref.cpu())
+
+
+def _run_bf16(ncz, p, o_dtype=torch.float32, producer="auto", splits=None):
+    dev = torch.device("cuda:0")
+    q, k, v = (torch.from_numpy(a.view(np.int16)).to(dev).view(torch.bfloat16) for a in (p.q, p.k, p.v))
+    o = torch.full((p.bh * p.strides[3],), SENTINEL, dtype=o_dtype, device=dev)
+    if splits is None:
+        ncz.launch_ex(q, k, v, o, C_opts(p), row_strides=p.row_strides, producer=producer)
+    else:
+        ncz.launch_splits(q, k, v, o, C_opts(p), splits, producer=producer)
+    assert ncz.sync_status() == 0
+    return o.float().cpu().numpy()
+
+
+BF16_CASES = [(2, 200, 64, True), (3, 333, 32, False), (2, 129, 16, True), (1, 1024, 64, False),
+              (4, 1000, 64, True)]
+
+
+@pytest.mark.parametrize("case", BF16_CASES, ids=lambda c: f"bh{c[0]}_s{c[1]}_d{c[2]}_c{int(c[3])}")
+@pytest.mark.parametrize("producer", ["tma", "lsu"])
+def test_bf16_inputs_match_oracle(ncz, oracle_mod, case, producer):
+    """bf16 Q/K/V (the kernel's bf16 variant: bf16 MMAs, P rounded to bf16)
+    against the oracle's bf16 path, within the bf16 bound; TMA = LSU bit-exact."""
+    bh, s, d, causal = case
+    p = C.normal_problem_bf16(bh, s, d, causal, 23, oracle_mod, std=0.8)
+    got = _run_bf16(ncz, p, producer=producer)
+    idx = C.active_index(p)
+    C.check(got, C.reference(p, oracle_mod), idx, f"bf16 {case} {producer}", atol=C.ATOL_BF16)
+    assert untouched(got, p, idx)
+    if producer == "lsu":
+        assert np.array_equal(got, _run_bf16(ncz, p, producer="tma"))
+
+
+@pytest.mark.parametrize("o_dtype", [torch.float16, torch.bfloat16])
+def test_bf16_inputs_16bit_outputs(ncz, oracle_mod, o_dtype):
+    p = C.normal_problem_bf16(3, 700, 64, True, 29, oracle_mod, std=0.7)
+    got = _run_bf16(ncz, p, o_dtype=o_dtype)
+    C.check(got, C.reference(p, oracle_mod), C.active_index(p), f"bf16 in, {o_dtype} out", atol=C.ATOL_BF16)
+
+
+def test_bf16_split_kv(ncz, oracle_mod):
+    p = C.normal_problem_bf16(1, 4096, 64, True, 31, oracle_mod, std=0.7)
+    got = _run_bf16(ncz, p, splits=4)
+    C.check(got, C.reference(p, oracle_mod), C.active_index(p), "bf16 split-KV", atol=C.ATOL_BF16)
+
+
+def test_bf16_output_from_f16_inputs(ncz, oracle_mod):
+    """bf16 O from f16 inputs (O type is independent of the input type)."""
+    p = C.normal_problem(2, 300, 32, False, 37, oracle_mod, std=0.7)
+    got = run(ncz, p, o_dtype="bfloat16")
+    C.check(got, C.reference(p, oracle_mod), C.active_index(p), "f16 in, bf16 out", atol=C.ATOL_BF16)

@@ -110,3 +110,25 @@ def test_oracle_pinned_to_reference_kernel(oracle_mod):
         assert abs(act.sum() - s1) <= 1e-6 * max(1.0, abs(s1)) + 1e-4
         assert abs((act ** 2).sum() - s2) <= 1e-6 * max(1.0, abs(s2)) + 1e-4
     assert worst <= 1e-5
+
+
+def test_bf16_oracle_matches_float64(oracle_mod):
+    """The bf16 input path of the oracle equals float64 attention on the same
+    bf16 values (decoded exactly) to f32 accuracy."""
+    bh, s, d = 2, 96, 32
+    q, k, v = (oracle_mod.fill_normal_bf16(bh * s * d, seed, 0.0, 0.7) for seed in (5, 6, 7))
+    out = oracle_mod.flash_reference(q, k, v, batch_heads=bh, seq_len=s, head_dim=d, q_stride=s * d,
+                                     k_stride=s * d, v_stride=s * d, o_stride=s * d, scale=0.2, causal=True)
+    qf, kf, vf = (oracle_mod.bf16_to_f32(a).reshape(bh, s, d).astype(np.float64) for a in (q, k, v))
+    sc = qf @ kf.transpose(0, 2, 1) * 0.2 + np.triu(np.full((s, s), -np.inf), 1)
+    pr = np.exp(sc - sc.max(-1, keepdims=True))
+    ref = (pr @ vf) / pr.sum(-1, keepdims=True)
+    assert np.abs(out.reshape(bh, s, d) - ref).max() < 1e-5
+
+
+def test_bf16_generator_rounds_to_nearest_even(oracle_mod):
+    h = oracle_mod.fill_normal(4096, 11, 0.0, 1.3)          # same stream, f16 rounding
+    b = oracle_mod.bf16_to_f32(oracle_mod.fill_normal_bf16(4096, 11, 0.0, 1.3))
+    assert np.abs(b - h.astype(np.float32)).max() <= 2.0 ** -7 * np.abs(b).max()
+    # bf16 values have no bits below the top 16
+    assert np.all((b.view(np.uint32) & 0xFFFF) == 0)
