@@ -280,6 +280,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--gather", action="store_true",
+                    help="N > 1: also time gathering every rank's O shard on rank 0 (NCCL over NVLink), "
+                         "separately from the metric")
     ap.add_argument("--splits", type=int, default=None,
                     help="force the split-KV count (ncz_flash_fwd_splits: 1 = none); default: automatic")
     args = ap.parse_args()
@@ -407,6 +410,28 @@ def main():
                "h2d_bytes_per_step": 3 * n * 2, "d2h_bytes_per_step": n * o.element_size(), "steps": args.e2e_steps,
                "api": "flash.launch_host -> ncz_flash_fwd_host (C ABI), default chunking"}
 
+    # Optional O gather to rank 0 over NVLink (NCCL), off the timed metric.
+    gather = None
+    if args.gather and dist is not None:
+        parts = [torch.empty_like(o) for _ in range(world)] if rank == 0 else None
+        for _ in range(2):
+            dist.gather(o, parts, dst=0)
+        barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 5
+        g0.record(stream)
+        for _ in range(reps):
+            dist.gather(o, parts, dst=0)
+        g1.record(stream)
+        barrier()
+        gt = torch.tensor([g0.elapsed_time(g1) / reps], dtype=torch.float64, device=dev)
+        dist.all_reduce(gt, op=dist.ReduceOp.MAX)
+        gms = float(gt.item())
+        moved = (world - 1) * n * o.element_size()
+        gather = {"ms": gms, "bytes_to_rank0": moved, "gbps_into_rank0": moved / (gms * 1e6),
+                  "how": "torch.distributed.gather of each rank's O shard to rank 0 (NCCL), max over ranks"}
+        del parts
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         tf, dt, what, fl, thr, _ = cpu_sample(oracle, hq, hk, hv, s, d, causal, scale, args.cpu_seconds, bh=bh)
@@ -436,9 +461,10 @@ def main():
             "roofline": {"bound": "tensor", "achieved": per_gpu, "peak": peak, "unit": "TFLOP/s",
                          "frac": per_gpu / peak, "traffic": traffic,
                          "peak_source": f"{src} bf16 {'sustained' if peak == sustained else 'burst'}",
-                         "kernel": f"ncz::flash_fwd_sm100<{d},true>"},
+                         "kernel": f"ncz::flash_fwd_sm100<{d},true,false>"},
             "cpu_baseline": cpu,
             "e2e": e2e,
+            "o_gather": gather,
             "gpu_launches": launches,
             "clocks": clocks,
         }

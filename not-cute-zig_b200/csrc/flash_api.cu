@@ -132,8 +132,8 @@ Resolved from_desc(const ncz_flash_desc &d) {
 bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 // 3-D map over one operand: dims (d, seq, bh), box (d, box_rows, 1), swizzle = row width.
-bool encode_map(CUtensorMap *map, const void *ptr, size_t d, size_t seq, size_t bh, size_t row, size_t slice,
-                uint32_t box_rows, bool bf16) {
+bool encode_map_uncached(CUtensorMap *map, const void *ptr, size_t d, size_t seq, size_t bh, size_t row,
+                         size_t slice, uint32_t box_rows, bool bf16) {
     cuuint64_t dims[3] = {d, seq, bh};
     cuuint64_t strides[2] = {row * 2, slice * 2};
     cuuint32_t box[3] = {static_cast<cuuint32_t>(d), box_rows, 1u};
@@ -145,6 +145,47 @@ bool encode_map(CUtensorMap *map, const void *ptr, size_t d, size_t seq, size_t 
                                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return res == CUDA_SUCCESS;
+}
+
+// Encoded maps, direct-mapped by their inputs.  A map is a pure function of
+// (address, layout, box, type), so a hit is always valid, also for a buffer
+// freed and reallocated at the same address.
+struct MapKey {
+    uintptr_t ptr;
+    size_t d, seq, bh, row, slice;
+    uint32_t box_rows, bf16;
+    bool operator==(const MapKey &o) const {
+        return ptr == o.ptr && d == o.d && seq == o.seq && bh == o.bh && row == o.row && slice == o.slice &&
+               box_rows == o.box_rows && bf16 == o.bf16;
+    }
+};
+struct MapSlot {
+    bool used = false;
+    MapKey key;
+    CUtensorMap map;
+};
+constexpr size_t kMapSlots = 256;
+MapSlot g_maps[kMapSlots];
+
+bool encode_map(CUtensorMap *map, const void *ptr, size_t d, size_t seq, size_t bh, size_t row, size_t slice,
+                uint32_t box_rows, bool bf16) {
+    const MapKey key{reinterpret_cast<uintptr_t>(ptr), d, seq, bh, row, slice, box_rows, bf16 ? 1u : 0u};
+    size_t h = key.ptr * 0x9E3779B97F4A7C15ull;
+    for (const size_t v : {d, seq, bh, row, slice, size_t(box_rows), size_t(key.bf16)}) h = (h ^ v) * 0x100000001B3ull;
+    MapSlot &slot = g_maps[(h >> 24) % kMapSlots];
+    {
+        std::lock_guard<std::mutex> lock(g_mu);
+        if (slot.used && slot.key == key) {
+            *map = slot.map;
+            return true;
+        }
+    }
+    if (!encode_map_uncached(map, ptr, d, seq, bh, row, slice, box_rows, bf16)) return false;
+    std::lock_guard<std::mutex> lock(g_mu);
+    slot.used = true;
+    slot.key = key;
+    slot.map = *map;
+    return true;
 }
 
 template <int D, bool kTma, bool kBf16>
@@ -535,6 +576,7 @@ int ncz_init(void) {
 int ncz_shutdown(void) {
     std::lock_guard<std::mutex> lock(g_mu);
     std::memset(g_attr_done, 0, sizeof(g_attr_done));
+    for (MapSlot &m : g_maps) m.used = false;
     g_init_done = false;
     g_init_status = NCZ_ERROR_NOT_INITIALIZED;
     g_encode = nullptr;
