@@ -32,6 +32,11 @@ using ncz::SmemLayout;
 constexpr int kMaxDevices = 64;
 constexpr size_t kGroupRows = static_cast<size_t>(ncz::kBlockM) * ncz::kQTiles;  // Q rows per CTA
 constexpr int kVariants = 12;  // (D in 16/32/64) x (TMA, LSU) x (f16, bf16 inputs)
+// Items with at least this many K tiles end their CTA instead of taking the
+// next item; measured fastest with every item taking the next one.
+#ifndef NCZ_WALK_TILES
+#define NCZ_WALK_TILES (1 << 30)
+#endif
 
 std::mutex g_mu;
 bool g_init_done = false;
@@ -384,8 +389,12 @@ int launch_on_current(const Resolved &r, int dev) {
         p.part_o = static_cast<float *>(ws);
         p.part_ml = p.part_o + rows * r.d;
     }
-    const unsigned grid =
-        static_cast<unsigned>(static_cast<size_t>(p.num_groups) * r.bh * static_cast<size_t>(p.num_splits));
+    // One CTA per work item, heaviest first; at most one is resident per SM (TMEM
+    // holds one CTA's 512 columns) and it takes over the items of CTAs that have
+    // not started yet.
+    const size_t items = static_cast<size_t>(p.num_groups) * r.bh * static_cast<size_t>(p.num_splits);
+    const unsigned grid = static_cast<unsigned>(items);
+    p.walk_tiles = NCZ_WALK_TILES;
     const bool bf = r.in_dtype == NCZ_DTYPE_BF16;
     int st;
     switch (r.d) {

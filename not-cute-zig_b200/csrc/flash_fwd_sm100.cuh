@@ -6,17 +6,28 @@
 // warp-specialised kernel, templated on head_dim (16/32/64) and on how tiles
 // reach shared memory (TMA, or plain loads for misaligned strides).
 //
-// Work unit: one CTA per (batch x head slice, pair of 128-row Q tiles).  Q
-// tile w covers rows q_base + 128 w .. + 127.  K/V stream through a
-// kStages-deep ring of 128-key tiles shared by both Q tiles of the CTA.
+// Work item: (batch x head slice, pair of 128-row Q tiles[, K range under
+// split-KV]); Q tile w covers rows q_base + 128 w .. + 127.  The grid has one
+// CTA per item (heaviest first), but a running CTA takes further items from
+// CTAs that have not started, through cluster launch control, so one CTA per
+// SM keeps pulling items in launch order.  Every role keeps running counters
+// across items: the next item's Q (double-buffered), K/V (a kStages-deep ring
+// of 128-key tiles shared by both Q tiles) and first scores are fetched while
+// the current item's last tiles and epilogue run.
+//
+// Two pipelines w = 0, 1 (an MMA warp, a softmax warpgroup, a TMEM quarter)
+// each take one Q tile per item: pipeline w takes Q tile w ^ (item count & 1).
+// Under causal masking Q tile 0 of an item has one K tile fewer than Q tile 1;
+// alternating keeps either pipeline from gaining a tile per item on the other
+// until the shared K/V ring stalls it.
 //
 // Warp roles (384 threads):
 //   warp 0       producer: TMA or LSU loads of Q, K, V
-//   warp 1       TMEM allocator + tcgen05 MMA issuer for Q tile 0
-//   warp 2       tcgen05 MMA issuer for Q tile 1
+//   warp 1       TMEM allocator + tcgen05 MMA issuer for pipeline 0
+//   warp 2       tcgen05 MMA issuer for pipeline 1
 //   (all run as whole warps; elect.sync picks the lane that issues)
 //   warp 3       idle (keeps the softmax warpgroups warpgroup-aligned)
-//   warpgroup 1+w softmax for Q tile w (thread = row = TMEM lane)
+//   warpgroup 1+w softmax for pipeline w (thread = row = TMEM lane)
 //
 // TMEM (512 columns): per Q tile w the scores S_w (128 cols f32, QK^T, M=128
 // N=128), the probabilities P_w (128 f16 keys = 64 cols, the A operand of PV
@@ -39,6 +50,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cstdint>
+#include <type_traits>
 
 #include "sm100_ptx.cuh"
 
@@ -48,6 +60,10 @@ constexpr int kBlockM = 128;  // rows per Q tile = TMEM lanes
 constexpr int kBlockN = 128;  // keys per K/V tile
 constexpr int kQTiles = 2;    // Q tiles per CTA
 constexpr int kThreads = 128 * (1 + kQTiles);
+// Launch-control response ring (next work items) and the warps that read each
+// response: the producer, the MMA warps and the softmax warps.
+constexpr int kClcSlots = 4;
+constexpr uint32_t kClcReaders = 1 + kQTiles + 4 * kQTiles;
 constexpr uint32_t kTmemCols = 512;
 // TMEM column map per Q tile w (base kTileCols * w): S | P | O
 constexpr uint32_t kColP = kBlockN;               // f16 pairs: kBlockN / 2 columns
@@ -69,11 +85,6 @@ constexpr unsigned long long kWaitLimitCycles = 4000000000ull;
 #endif
 constexpr int kExp2EmuPeriod = NCZ_EXP2_EMU_PERIOD;
 constexpr int kExp2EmuCount = NCZ_EXP2_EMU_COUNT;
-// 1: the two softmax warps of an SM sub-partition take turns on its MUFU unit.
-#ifndef NCZ_EXP_TURNS
-#define NCZ_EXP_TURNS 0
-#endif
-constexpr bool kExpTurns = NCZ_EXP_TURNS != 0;
 
 // where a bounded wait gave up (bits 24..30 of the status word)
 enum WaitSite : uint32_t {
@@ -87,7 +98,10 @@ enum WaitSite : uint32_t {
     kSiteODone = 8,
     kSiteMmaDrain = 9,
     kSiteProducerDrain = 10,
-    kSiteTurn = 11,
+    kSiteQEmpty = 11,
+    kSiteOFree = 13,
+    kSiteClcFull = 14,
+    kSiteClcEmpty = 15,
 };
 
 struct FlashParams {
@@ -110,6 +124,9 @@ struct FlashParams {
     // part_ml [split][slice][row][2] for combine_splits.  1 = direct output.
     int num_splits;
     int kv_per_split;
+    // A CTA takes a further item (launch control) only while its current item
+    // has fewer than walk_tiles K tiles; heavier items end their CTA.
+    int walk_tiles;
     float *part_o;
     float *part_ml;
 };
@@ -123,27 +140,32 @@ struct SmemLayout {
     static constexpr int kStagesRaw = (D == 64 ? 128 * 1024 : 64 * 1024) / (2 * kKvTile);
     static constexpr int kStages = kStagesRaw > 8 ? 8 : kStagesRaw;
     static constexpr uint32_t kUmmaLayout = D == 64 ? 2u : (D == 32 ? 4u : 6u);
+    static constexpr int kQSlot = kQTiles * kQTile;  // Q of one item; two slots
     static constexpr int kOffQ = 0;
-    static constexpr int kOffK = kOffQ + kQTiles * kQTile;
+    static constexpr int kOffK = kOffQ + 2 * kQSlot;
     static constexpr int kOffV = kOffK + kStages * kKvTile;
     static constexpr int kOffBar = kOffV + kStages * kKvTile;
-    // barriers: q_full | k_full[S] | v_full[S] | kv_empty[S] | s_full[Q] | s_free[Q] | p_full[Q] | o_done[Q]
-    //           | drain[Q] | turn[4][Q]
+    // barriers: q_full[2] | q_empty[2] | k_full[S] | v_full[S] | kv_empty[S] | s_full[Q] | s_free[Q]
+    //           | p_full[Q] | o_done[Q] | o_free[Q] | drain[Q] | clc_full[C] | clc_empty[C]
     static constexpr int kBarQFull = 0;
-    static constexpr int kBarKFull = 1;
+    static constexpr int kBarQEmpty = 2;
+    static constexpr int kBarKFull = 4;
     static constexpr int kBarVFull = kBarKFull + kStages;
     static constexpr int kBarKvEmpty = kBarVFull + kStages;
     static constexpr int kBarSFull = kBarKvEmpty + kStages;
     static constexpr int kBarSFree = kBarSFull + kQTiles;
     static constexpr int kBarPFull = kBarSFree + kQTiles;
     static constexpr int kBarODone = kBarPFull + kQTiles;
-    static constexpr int kBarDrain = kBarODone + kQTiles;  // one per MMA warp
-    // turn[i][w]: Q tile w's softmax warp on sub-partition i may use the MUFU unit
-    static constexpr int kBarTurn = kBarDrain + kQTiles;
-    static constexpr int kNumBars = kBarTurn + 4 * kQTiles;
-    static constexpr int kOffTmemSlot = kOffBar + kNumBars * 8;
+    static constexpr int kBarOFree = kBarODone + kQTiles;
+    static constexpr int kBarDrain = kBarOFree + kQTiles;  // one per MMA warp
+    static constexpr int kBarClcFull = kBarDrain + kQTiles;
+    static constexpr int kBarClcEmpty = kBarClcFull + kClcSlots;
+    static constexpr int kNumBars = kBarClcEmpty + kClcSlots;
+    static constexpr int kOffClc = (kOffBar + kNumBars * 8 + 15) / 16 * 16;  // 16-byte launch-control responses
+    static constexpr int kOffTmemSlot = kOffClc + 16 * kClcSlots;
     static constexpr int kOffAbort = kOffTmemSlot + 4;
-    static constexpr int kBytes = kOffAbort + 4;
+    static constexpr int kOffStash = kOffAbort + 4;  // per warp: item walk state (2 ints)
+    static constexpr int kBytes = kOffStash + 8 * (kThreads / 32);
     static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
     static_assert(kStages >= 2, "K/V ring");
     static_assert(kAlloc <= 227 * 1024, "shared memory");
@@ -166,9 +188,8 @@ __device__ unsigned long long g_ncz_wait_limit = kWaitLimitCycles;
 // signals its first scores, so the softmax's bounded wait runs out.
 __device__ int g_ncz_test_drop = 0;
 
-__device__ __forceinline__ Work make_work(const FlashParams &p) {
+__device__ __forceinline__ Work make_work(const FlashParams &p, int item) {
     Work wk;
-    const int item = static_cast<int>(blockIdx.x);
     // Heaviest (last) Q-tile groups first: under causal masking they visit the most K tiles.
     const int per_group = p.batch_heads * p.num_splits;
     const int group = p.num_groups - 1 - item / per_group;
@@ -233,7 +254,8 @@ struct Bars {
     using L = SmemLayout<D>;
     uint32_t base;
     __device__ __forceinline__ uint32_t at(int i) const { return base + L::kOffBar + 8u * i; }
-    __device__ __forceinline__ uint32_t q_full() const { return at(L::kBarQFull); }
+    __device__ __forceinline__ uint32_t q_full(int slot) const { return at(L::kBarQFull + slot); }
+    __device__ __forceinline__ uint32_t q_empty(int slot) const { return at(L::kBarQEmpty + slot); }
     __device__ __forceinline__ uint32_t k_full(int s) const { return at(L::kBarKFull + s); }
     __device__ __forceinline__ uint32_t v_full(int s) const { return at(L::kBarVFull + s); }
     __device__ __forceinline__ uint32_t kv_empty(int s) const { return at(L::kBarKvEmpty + s); }
@@ -241,60 +263,115 @@ struct Bars {
     __device__ __forceinline__ uint32_t s_free(int w) const { return at(L::kBarSFree + w); }
     __device__ __forceinline__ uint32_t p_full(int w) const { return at(L::kBarPFull + w); }
     __device__ __forceinline__ uint32_t o_done(int w) const { return at(L::kBarODone + w); }
+    __device__ __forceinline__ uint32_t o_free(int w) const { return at(L::kBarOFree + w); }
     __device__ __forceinline__ uint32_t drain(int w) const { return at(L::kBarDrain + w); }
-    __device__ __forceinline__ uint32_t turn(int sub, int w) const { return at(L::kBarTurn + kQTiles * sub + w); }
+    __device__ __forceinline__ uint32_t clc_full(int s) const { return at(L::kBarClcFull + s); }
+    __device__ __forceinline__ uint32_t clc_empty(int s) const { return at(L::kBarClcEmpty + s); }
+    __device__ __forceinline__ uint32_t clc_resp(int s) const { return base + L::kOffClc + 16u * s; }
 };
+
+// ---------------------------------------------------------------------------
+// work-item walk
+// ---------------------------------------------------------------------------
+// A CTA's first item is its blockIdx.x.  While item i runs, the producer asks
+// cluster launch control to cancel a CTA of this grid that has not started and
+// takes that CTA's item as item i + 1.  Items leave the hardware queue in
+// launch order (heaviest first), so every SM keeps pulling the next heaviest
+// item as soon as it can take one, and the next item's Q, K/V and first scores
+// load while the current item's last tiles and epilogue run.  The response for
+// item i + 1 lands in ring slot i % kClcSlots; every reader warp decodes it and
+// releases the slot.  A request that finds no CTA left ends the walk (no
+// request follows a failed one).
+template <int D>
+__device__ __forceinline__ bool request_item(const Bars<D> &b, int i, volatile uint32_t *abort_flag) {
+    const int s = i % kClcSlots;
+    if (i >= kClcSlots && !warp_wait(b.clc_empty(s), ((i / kClcSlots) - 1) & 1, abort_flag, kSiteClcEmpty))
+        return false;
+    clc_try_cancel_elect(b.clc_resp(s), b.clc_full(s));
+    return true;
+}
+
+// Item i (i >= 1) of the CTA's walk; -1 when the walk is over, -2 when the
+// wait gave up (the CTA is aborting).
+template <int D>
+__device__ __forceinline__ int take_item(const Bars<D> &b, int i, volatile uint32_t *abort_flag, int lane) {
+    const int s = (i - 1) % kClcSlots;
+    if (!warp_wait(b.clc_full(s), ((i - 1) / kClcSlots) & 1, abort_flag, kSiteClcFull)) return -2;
+    const int item = clc_decode(b.clc_resp(s));
+    fence_proxy_async_smem();  // the read precedes the slot's next (async-proxy) write
+    __syncwarp();
+    if (lane == 0) mbar_arrive(b.clc_empty(s));
+    return item;
+}
 
 // ---------------------------------------------------------------------------
 // producer, TMA variant (whole warp; elect.sync picks the issuing lane)
 // ---------------------------------------------------------------------------
-// Loads that need no free-slot wait: Q and the first min(kStages, n_max) K/V
-// tiles.  Runs before the CTA-wide barrier that publishes the TMEM address, so
-// these copies overlap the TMEM allocation.  Returns the number of K/V tiles issued.
+// Per item: Q into slot it & 1 once the item two back released it, the
+// request for the next item, then the item's K/V tiles through the ring (tile
+// counter t runs across items).
 template <int D>
-__device__ __forceinline__ int producer_tma_prologue(const CUtensorMap *tq, const CUtensorMap *tk,
-                                                     const CUtensorMap *tv, uint32_t sbase, const Work &wk) {
+__device__ __forceinline__ void producer_tma(const FlashParams &p, const CUtensorMap *tq, const CUtensorMap *tk,
+                                             const CUtensorMap *tv, uint32_t sbase, volatile uint32_t *abort_flag,
+                                             int lane) {
     using L = SmemLayout<D>;
     const Bars<D> b{sbase};
-    uint32_t qbytes = 0;
-#pragma unroll
-    for (int w = 0; w < kQTiles; ++w) qbytes += wk.n[w] > 0 ? L::kQTile : 0;
-    mbar_arrive_expect_tx_elect(b.q_full(), qbytes);
-#pragma unroll
-    for (int w = 0; w < kQTiles; ++w)
-        if (wk.n[w] > 0)
-            tma_load_3d_elect(sbase + L::kOffQ + w * L::kQTile, tq, b.q_full(), 0, wk.q_base + w * kBlockM, wk.slice);
-    const int first = wk.n_max < L::kStages ? wk.n_max : L::kStages;
-    for (int j = 0; j < first; ++j) {
-        mbar_arrive_expect_tx_elect(b.k_full(j), L::kKvTile);
-        tma_load_3d_elect(sbase + L::kOffK + j * L::kKvTile, tk, b.k_full(j), 0, (wk.kv0 + j) * kBlockN, wk.slice);
-        mbar_arrive_expect_tx_elect(b.v_full(j), L::kKvTile);
-        tma_load_3d_elect(sbase + L::kOffV + j * L::kKvTile, tv, b.v_full(j), 0, (wk.kv0 + j) * kBlockN, wk.slice);
-    }
-    return first;
-}
-
-// The remaining K/V tiles (from j_begin), each after its ring slot is released.
-template <int D>
-__device__ __forceinline__ void producer_tma(const CUtensorMap *tk, const CUtensorMap *tv, uint32_t sbase,
-                                             const Work &wk, int j_begin, volatile uint32_t *abort_flag) {
-    using L = SmemLayout<D>;
-    const Bars<D> b{sbase};
-    int j = j_begin;
-    for (; j < wk.n_max; ++j) {
-        const int st = j % L::kStages;
-        if (j >= L::kStages && !warp_wait(b.kv_empty(st), ((j / L::kStages) - 1) & 1, abort_flag, kSiteKvEmpty))
+    uint32_t t = 0;    // K/V tiles issued so far
+    int it = 0;        // items started
+    int pending = -1;  // items started when the unanswered launch-control request was made
+    bool ok = true;
+    for (int item = static_cast<int>(blockIdx.x); ok && item >= 0;) {
+        const Work wk = make_work(p, item);
+        const int qs = it & 1;
+        if (it >= 2 && !warp_wait(b.q_empty(qs), ((it >> 1) - 1) & 1, abort_flag, kSiteQEmpty)) {
+            ok = false;
             break;
-        mbar_arrive_expect_tx_elect(b.k_full(st), L::kKvTile);
-        tma_load_3d_elect(sbase + L::kOffK + st * L::kKvTile, tk, b.k_full(st), 0, (wk.kv0 + j) * kBlockN, wk.slice);
-        mbar_arrive_expect_tx_elect(b.v_full(st), L::kKvTile);
-        tma_load_3d_elect(sbase + L::kOffV + st * L::kKvTile, tv, b.v_full(st), 0, (wk.kv0 + j) * kBlockN, wk.slice);
+        }
+        uint32_t qbytes = 0;
+#pragma unroll
+        for (int w = 0; w < kQTiles; ++w) qbytes += wk.n[w] > 0 ? L::kQTile : 0;
+        mbar_arrive_expect_tx_elect(b.q_full(qs), qbytes);
+#pragma unroll
+        for (int w = 0; w < kQTiles; ++w)
+            if (wk.n[w] > 0)
+                tma_load_3d_elect(sbase + L::kOffQ + qs * L::kQSlot + w * L::kQTile, tq, b.q_full(qs), 0,
+                                  wk.q_base + w * kBlockM, wk.slice);
+        const int cur = it++;
+        const bool walk = wk.n_max < p.walk_tiles;
+        if (walk) {
+            if (!request_item(b, cur, abort_flag)) {
+                ok = false;
+                break;
+            }
+            pending = cur;
+        }
+        for (int j = 0; j < wk.n_max; ++j, ++t) {
+            const int st = t % L::kStages;
+            if (t >= L::kStages && !warp_wait(b.kv_empty(st), ((t / L::kStages) - 1) & 1, abort_flag, kSiteKvEmpty)) {
+                ok = false;
+                break;
+            }
+            mbar_arrive_expect_tx_elect(b.k_full(st), L::kKvTile);
+            tma_load_3d_elect(sbase + L::kOffK + st * L::kKvTile, tk, b.k_full(st), 0, (wk.kv0 + j) * kBlockN,
+                              wk.slice);
+            mbar_arrive_expect_tx_elect(b.v_full(st), L::kKvTile);
+            tma_load_3d_elect(sbase + L::kOffV + st * L::kKvTile, tv, b.v_full(st), 0, (wk.kv0 + j) * kBlockN,
+                              wk.slice);
+        }
+        if (!ok) break;
+        item = walk ? take_item(b, it, abort_flag, lane) : -1;
+        if (item != -2) pending = -1;
     }
-    // Every issued copy must land before shared memory is released.
-    bounded_wait(b.q_full(), 0, abort_flag, kSiteProducerDrain, false);
-    for (int t = j - L::kStages < 0 ? 0 : j - L::kStages; t < j; ++t) {
-        const int st = t % L::kStages;
-        const uint32_t ph = (t / L::kStages) & 1;
+    // Every issued copy must land before shared memory is released: the Q of the
+    // last two items, the last kStages K/V tiles and an unanswered request.
+    for (int i = it - 2 < 0 ? 0 : it - 2; i < it; ++i)
+        bounded_wait(b.q_full(i & 1), (i >> 1) & 1, abort_flag, kSiteProducerDrain, false);
+    if (pending >= 0)
+        bounded_wait(b.clc_full(pending % kClcSlots), (pending / kClcSlots) & 1, abort_flag, kSiteProducerDrain,
+                     false);
+    for (uint32_t u = t < static_cast<uint32_t>(L::kStages) ? 0u : t - L::kStages; u < t; ++u) {
+        const int st = u % L::kStages;
+        const uint32_t ph = (u / L::kStages) & 1;
         bounded_wait(b.k_full(st), ph, abort_flag, kSiteProducerDrain, false);
         bounded_wait(b.v_full(st), ph, abort_flag, kSiteProducerDrain, false);
     }
@@ -327,110 +404,172 @@ __device__ __forceinline__ void lsu_tile(uint8_t *dst, const uint16_t *src, long
 }
 
 template <int D>
-__device__ __forceinline__ void producer_lsu(const FlashParams &p, uint8_t *smem, uint32_t sbase, const Work &wk,
+__device__ __forceinline__ void producer_lsu(const FlashParams &p, uint8_t *smem, uint32_t sbase,
                                              volatile uint32_t *abort_flag, int lane) {
     using L = SmemLayout<D>;
     const Bars<D> b{sbase};
-    const uint16_t *qs = p.q + wk.slice * p.q_stride;
-    const uint16_t *ks = p.k + wk.slice * p.k_stride;
-    const uint16_t *vs = p.v + wk.slice * p.v_stride;
+    uint32_t t = 0;    // K/V tiles loaded so far
+    int it = 0;        // items started
+    int pending = -1;  // items started when the unanswered launch-control request was made
+    bool ok = true;
+    for (int item = static_cast<int>(blockIdx.x); ok && item >= 0;) {
+        const Work wk = make_work(p, item);
+        const uint16_t *qs = p.q + wk.slice * p.q_stride;
+        const uint16_t *ks = p.k + wk.slice * p.k_stride;
+        const uint16_t *vs = p.v + wk.slice * p.v_stride;
+        const int slot = it & 1;
+        if (it >= 2 && !warp_wait(b.q_empty(slot), ((it >> 1) - 1) & 1, abort_flag, kSiteQEmpty)) break;
+        const int cur = it++;
+        const bool walk = wk.n_max < p.walk_tiles;
+        if (walk) {
+            if (!request_item(b, cur, abort_flag)) break;
+            pending = cur;
+        }
 #pragma unroll
-    for (int w = 0; w < kQTiles; ++w)
-        if (wk.n[w] > 0)
-            lsu_tile<D, kBlockM>(smem + L::kOffQ + w * L::kQTile, qs, p.q_row, wk.q_base + w * kBlockM, p.seq_len,
+        for (int w = 0; w < kQTiles; ++w)
+            if (wk.n[w] > 0)
+                lsu_tile<D, kBlockM>(smem + L::kOffQ + slot * L::kQSlot + w * L::kQTile, qs, p.q_row,
+                                     wk.q_base + w * kBlockM, p.seq_len, lane);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(b.q_full(slot));
+        for (int j = 0; j < wk.n_max; ++j, ++t) {
+            const int st = t % L::kStages;
+            if (t >= L::kStages && !warp_wait(b.kv_empty(st), ((t / L::kStages) - 1) & 1, abort_flag, kSiteKvEmpty)) {
+                ok = false;
+                break;
+            }
+            lsu_tile<D, kBlockN>(smem + L::kOffK + st * L::kKvTile, ks, p.k_row, (wk.kv0 + j) * kBlockN, p.seq_len,
                                  lane);
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(b.q_full());
-    for (int j = 0; j < wk.n_max; ++j) {
-        const int st = j % L::kStages;
-        if (j >= L::kStages && !warp_wait(b.kv_empty(st), ((j / L::kStages) - 1) & 1, abort_flag, kSiteKvEmpty))
-            break;
-        lsu_tile<D, kBlockN>(smem + L::kOffK + st * L::kKvTile, ks, p.k_row, (wk.kv0 + j) * kBlockN, p.seq_len, lane);
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(b.k_full(st));
-        lsu_tile<D, kBlockN>(smem + L::kOffV + st * L::kKvTile, vs, p.v_row, (wk.kv0 + j) * kBlockN, p.seq_len, lane);
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(b.v_full(st));
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(b.k_full(st));
+            lsu_tile<D, kBlockN>(smem + L::kOffV + st * L::kKvTile, vs, p.v_row, (wk.kv0 + j) * kBlockN, p.seq_len,
+                                 lane);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(b.v_full(st));
+        }
+        if (!ok) break;
+        item = walk ? take_item(b, it, abort_flag, lane) : -1;
+        if (item != -2) pending = -1;
     }
+    // An unanswered request must land before shared memory is released.
+    if (pending >= 0)
+        bounded_wait(b.clc_full(pending % kClcSlots), (pending / kClcSlots) & 1, abort_flag, kSiteProducerDrain,
+                     false);
+    __syncwarp();
 }
 
 // ---------------------------------------------------------------------------
 // MMA issuer (whole warp; elect.sync picks the issuing lane)
 // ---------------------------------------------------------------------------
+// QK^T of ring tile t (K in stage t % kStages) for one Q tile into its S.
 template <int D, bool kBf16>
-__device__ __forceinline__ void issue_qk(int j, uint32_t sbase, uint32_t tS, uint64_t qdesc) {
+__device__ __forceinline__ void issue_qk(uint32_t t, uint32_t sbase, uint32_t tS, uint64_t qdesc) {
     using L = SmemLayout<D>;
     constexpr uint32_t idesc_qk = umma_idesc_f16_f32(kBlockM, kBlockN, 0, 0, kBf16);  // both K-major
-    const int st = j % L::kStages;
+    const int st = t % L::kStages;
     const uint64_t kdesc = umma_smem_desc(sbase + L::kOffK + st * L::kKvTile, 16, 8 * L::kSpan, L::kUmmaLayout);
     // K advance: 32 bytes (2 encoded units) inside the swizzled row per step
     umma_ss_chain_elect<D / 16>(tS, qdesc, kdesc, idesc_qk);
 }
 
+// O (+)= P V of ring tile t; `first` starts the accumulation of a new item.
 template <int D, bool kBf16>
-__device__ __forceinline__ void issue_pv(int j, uint32_t sbase, uint32_t tP, uint32_t tO) {
+__device__ __forceinline__ void issue_pv(uint32_t t, bool first, uint32_t sbase, uint32_t tP, uint32_t tO) {
     using L = SmemLayout<D>;
     constexpr uint32_t idesc_pv = umma_idesc_f16_f32(kBlockM, D, 0, 1, kBf16);  // B = V, MN-major
-    const int st = j % L::kStages;
+    const int st = t % L::kStages;
     // V tile: kBlockN keys x D, rows of 2D bytes (one swizzle atom wide); 8-row groups 8*span apart.
     const uint64_t vdesc =
         umma_smem_desc(sbase + L::kOffV + st * L::kKvTile, L::kKvTile, 8 * L::kSpan, L::kUmmaLayout);
     // 16 keys per step: 8 TMEM columns of P, 16 rows of V
     umma_ts_chain_elect<kBlockN / 16>(tO, tP, vdesc, static_cast<uint64_t>((16 * L::kSpan) >> 4), idesc_pv,
-                                      j > 0 ? 1u : 0u);
+                                      first ? 0u : 1u);
 }
 
-// One MMA warp per Q tile w (warps 1 and 2).  Per K tile j: QK_w(j+1) as soon
-// as the softmax has read S_w(j) and K(j+1) is resident, then PV_w(j) once
-// P_w(j) is stored and V(j) is resident.  Each warp arrives once per K tile on
-// the stage's kv_empty barrier (a commit after its PV, or a plain arrive past
-// its causal range), so a stage is released when both Q tiles are done with it.
+// One MMA warp per Q tile w (warps 1 and 2), over all of the CTA's items.  Per
+// K tile j of an item: QK_w(j+1) as soon as the softmax has read S_w(j) and
+// K(j+1) is resident, then PV_w(j) once P_w(j) is stored and V(j) is resident;
+// the first PV of an item also waits until the softmax has read the previous
+// item's O (o_free).  After its item's last QK the warp counts itself out of
+// the Q slot (q_empty).  Each warp arrives once per K tile on the stage's
+// kv_empty barrier (a commit after its PV, or a plain arrive past its causal
+// range), so a stage is released when both Q tiles are done with it.
 template <int D, bool kBf16>
-__device__ __forceinline__ void mma_role(int w, uint32_t sbase, uint32_t tmem, const Work &wk,
+__device__ __forceinline__ void mma_role(const FlashParams &p, int w, uint32_t sbase, uint32_t tmem,
                                          volatile uint32_t *abort_flag, int lane) {
     using L = SmemLayout<D>;
+    constexpr int S = L::kStages;
     const Bars<D> b{sbase};
-    const int n = wk.n[w];
     const uint32_t tS = tmem + w * kTileCols, tP = tS + kColP, tO = tS + kColO;
-    const uint64_t qdesc = umma_smem_desc(sbase + L::kOffQ + w * L::kQTile, 16, 8 * L::kSpan, L::kUmmaLayout);
-    bool ok = true;
-    if (n > 0) {
-        ok = warp_wait(b.q_full(), 0, abort_flag, kSiteQFull) && warp_wait(b.k_full(0), 0, abort_flag, kSiteKFull);
-        if (ok) {
-            tc_fence_after();
-            issue_qk<D, kBf16>(0, sbase, tS, qdesc);
-            if (!(w == 0 && g_ncz_test_drop != 0)) umma_commit_elect(b.s_full(w));
-        }
-    }
-    int j = 0;
-    for (; ok && j < n; ++j) {
-        const int st = j % L::kStages;
-        if (j + 1 < n) {
-            const int st1 = (j + 1) % L::kStages;
-            ok = warp_wait(b.s_free(w), j & 1, abort_flag, kSiteSFree) &&
-                 warp_wait(b.k_full(st1), ((j + 1) / L::kStages) & 1, abort_flag, kSiteKFull);
-            if (!ok) break;
-            tc_fence_after();
-            issue_qk<D, kBf16>(j + 1, sbase, tS, qdesc);
-            umma_commit_elect(b.s_full(w));
-        }
-        ok = warp_wait(b.v_full(st), (j / L::kStages) & 1, abort_flag, kSiteVFull) &&
-             warp_wait(b.p_full(w), j & 1, abort_flag, kSitePFull);
+    uint32_t t = 0;    // ring tiles passed (all items)
+    uint32_t sc = 0;   // K tiles of this Q tile so far: S/P/O barrier phases
+    uint32_t epi = 0;  // items in which this Q tile had work: o_free phases
+    bool ok = true, walk = false;
+    for (int item = static_cast<int>(blockIdx.x), it = 0; ok && item >= 0;
+         ++it, item = ok && walk ? take_item(b, it, abort_flag, lane) : -1) {
+        const Work wk = make_work(p, item);
+        walk = wk.n_max < p.walk_tiles;
+        const int wq = w ^ (it & 1);  // Q tile of the item this pipeline takes
+        const int n = wq ? wk.n[1] : wk.n[0];  // a select keeps Work out of local memory
+        const int qs = it & 1;
+        // Waited for every item, also without work: this warp's q_empty arrivals
+        // then never run two phases ahead of the producer.
+        ok = warp_wait(b.q_full(qs), (it >> 1) & 1, abort_flag, kSiteQFull);
         if (!ok) break;
         tc_fence_after();
-        issue_pv<D, kBf16>(j, sbase, tP, tO);
-        umma_commit_elect(b.o_done(w));
-        umma_commit_elect(b.kv_empty(st));  // this Q tile is done with K(j) and V(j)
-    }
-    // K tiles beyond this Q tile's causal range: release them on its behalf, once
-    // each is loaded (so the arrival counts toward that tile's use of the stage).
-    for (; ok && j < wk.n_max; ++j) {
-        ok = warp_wait(b.k_full(j % L::kStages), (j / L::kStages) & 1, abort_flag, kSiteKFull);
-        if (ok && lane == 0) mbar_arrive(b.kv_empty(j % L::kStages));
-        __syncwarp();
+        const uint64_t qdesc =
+            umma_smem_desc(sbase + L::kOffQ + qs * L::kQSlot + wq * L::kQTile, 16, 8 * L::kSpan, L::kUmmaLayout);
+        if (n > 0) {
+            ok = (sc == 0 || warp_wait(b.s_free(w), (sc - 1) & 1, abort_flag, kSiteSFree)) &&
+                 warp_wait(b.k_full(t % S), (t / S) & 1, abort_flag, kSiteKFull);
+            if (!ok) break;
+            tc_fence_after();
+            issue_qk<D, kBf16>(t, sbase, tS, qdesc);
+            if (!(w == 0 && g_ncz_test_drop != 0)) umma_commit_elect(b.s_full(w));
+            if (n == 1) umma_commit_elect(b.q_empty(qs));
+        } else {
+            __syncwarp();
+            if (lane == 0) mbar_arrive(b.q_empty(qs));
+            __syncwarp();
+        }
+        int j = 0;
+        for (; ok && j < n; ++j) {
+            const uint32_t tj = t + j;
+            const int st = tj % S;
+            if (j + 1 < n) {
+                ok = warp_wait(b.s_free(w), (sc + j) & 1, abort_flag, kSiteSFree) &&
+                     warp_wait(b.k_full((tj + 1) % S), ((tj + 1) / S) & 1, abort_flag, kSiteKFull);
+                if (!ok) break;
+                tc_fence_after();
+                issue_qk<D, kBf16>(tj + 1, sbase, tS, qdesc);
+                umma_commit_elect(b.s_full(w));
+                if (j + 2 == n) umma_commit_elect(b.q_empty(qs));  // the item's last QK
+            }
+            ok = warp_wait(b.v_full(st), (tj / S) & 1, abort_flag, kSiteVFull) &&
+                 warp_wait(b.p_full(w), (sc + j) & 1, abort_flag, kSitePFull) &&
+                 (j > 0 || epi == 0 || warp_wait(b.o_free(w), (epi - 1) & 1, abort_flag, kSiteOFree));
+            if (!ok) break;
+            tc_fence_after();
+            issue_pv<D, kBf16>(tj, j == 0, sbase, tP, tO);
+            umma_commit_elect(b.o_done(w));
+            umma_commit_elect(b.kv_empty(st));  // this Q tile is done with K(tj) and V(tj)
+        }
+        // K tiles beyond this Q tile's causal range: release them on its behalf, once
+        // each is loaded (so the arrival counts toward that tile's use of the stage).
+        for (; ok && j < wk.n_max; ++j) {
+            const uint32_t tj = t + j;
+            ok = warp_wait(b.k_full(tj % S), (tj / S) & 1, abort_flag, kSiteKFull);
+            if (ok && lane == 0) mbar_arrive(b.kv_empty(tj % S));
+            __syncwarp();
+        }
+        if (n > 0) {
+            sc += n;
+            ++epi;
+        }
+        t += wk.n_max;
     }
     // All issued MMAs must finish before TMEM and shared memory are released.
     umma_commit_elect(b.drain(w));
@@ -593,107 +732,117 @@ __device__ __forceinline__ void prep_scores(float (&x)[kBlockN], bool pre_scale,
 }
 
 template <int D, bool kBf16>
-__device__ __forceinline__ void softmax_role(const FlashParams &p, uint32_t sbase, uint32_t tmem, const Work &wk,
+__device__ __forceinline__ void softmax_role(const FlashParams &p, uint8_t *smem, uint32_t sbase, uint32_t tmem,
                                              volatile uint32_t *abort_flag, int warp, int lane) {
+    using L = SmemLayout<D>;
     const Bars<D> b{sbase};
-    const int w = (warp - 4) >> 2;                                // Q tile of this warpgroup
+    const int w = (warp - 4) >> 2;                                // pipeline of this warpgroup
     const int sub = warp & 3;                                     // SM sub-partition
     const int r = static_cast<int>(threadIdx.x) - 128 * (w + 1);  // row inside the tile = TMEM lane
     const uint32_t tS = tmem + (static_cast<uint32_t>(sub * 32) << 16) + w * kTileCols;
     const uint32_t tP = tS + kColP, tO = tS + kColO;
-    const int n = wk.n[w];
-    const int n_other = wk.n[w ^ 1];
-    const int row = wk.q_base + w * kBlockM + r;
     const int seq_len = p.seq_len;
     // scale > 0: mask raw scores, exponent = fma(s, scale*log2e, -m).
     // Otherwise scale first, then mask, exponent = fma(x, 1, -m).
     const bool pre_scale = !(p.scale_log2 > 0.0f);
     const float kmul = pre_scale ? 1.0f : p.scale_log2;
-
-    float m = -INFINITY;  // exponent base: scaled row max, log2 domain (stale by < 8)
-    float l = 0.0f;       // running sum of 2^(x - m)
-    bool ok = true;
-    for (int j = 0; j < n; ++j) {
-        ok = warp_wait(b.s_full(w), j & 1, abort_flag, kSiteSFull);
-        if (!ok) break;
-        tc_fence_after();
-        float x[kBlockN];
+    // The walk state (item, items started) waits in shared memory while the
+    // tile loop runs, so it holds no registers there.
+    volatile int *stash = reinterpret_cast<volatile int *>(smem + L::kOffStash + 8 * warp);
+    uint32_t ph = 0;  // parity of the K tiles of this pipeline so far (all items): barrier phases
+    bool ok = true, walk = false;
+    for (int item = static_cast<int>(blockIdx.x), it = 0; ok && item >= 0;
+         ++it, item = ok && walk ? take_item(b, it, abort_flag, lane) : -1) {
+        int n, row, kv0, diag;
         {
-            uint32_t sr[kBlockN];
-            tmem_ld_x128_wait(tS, sr);
-#pragma unroll
-            for (int c = 0; c < kBlockN; ++c) x[c] = __uint_as_float(sr[c]);
+            const Work wk = make_work(p, item);
+            walk = wk.n_max < p.walk_tiles;
+            const int wq = w ^ (it & 1);  // Q tile of the item this pipeline takes
+            n = wq ? wk.n[1] : wk.n[0];
+            row = wk.q_base + wq * kBlockM + r;
+            kv0 = wk.kv0;
+            diag = wq ? wk.diag[1] : wk.diag[0];
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(b.s_free(w));  // S may be overwritten by the next QK^T
-        const int jg = wk.kv0 + j;  // K tile index in the sequence
-        prep_scores<0>(x, pre_scale, p.scale_log2, jg == wk.diag[w], lim_of(p, row, jg));
-        prep_scores<1>(x, pre_scale, p.scale_log2, jg == wk.diag[w], lim_of(p, row, jg));
-        float mx[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) mx[i] = fmaxf(x[i], x[8 + i]);
-#pragma unroll
-        for (int c = 16; c < kBlockN; c += 16) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) mx[i] = fmax3(mx[i], x[c + i], x[c + 8 + i]);
-        }
-        const float m_tile = fmaxf(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], fmax3(mx[5], mx[6], mx[7])));
-        const float m_new = fmaxf(m, m_tile * kmul);
-        const bool need = m_new > m + kRescaleThreshold;
-        float m_use = need ? m_new : m;
-        m_use = m_use == -INFINITY ? 0.0f : m_use;  // row with nothing visible yet
-
-        // The two softmax warps of a sub-partition (Q tiles 0 and 1) share its MUFU
-        // unit; optionally they take turns: tile j of Q tile 0, tile j of Q tile 1, ...
-        if (kExpTurns && (w == 0 ? (j >= 1 && j - 1 < n_other) : (j < n_other))) {
-            ok = warp_wait(b.turn(sub, w), (w == 0 ? j - 1 : j) & 1, abort_flag, kSiteTurn);
-            if (!ok) break;
-        }
-        uint32_t pk[kBlockN / 2];
-        const float tsum = exp_row<kBf16>(x, kmul, m_use, pk);
-        if (kExpTurns && (w == 0 ? (j < n_other) : (j + 1 < n_other))) {
-            __syncwarp();
-            if (lane == 0) mbar_arrive(b.turn(sub, w ^ 1));
-        }
-        const float alpha = ex2_approx(m - m_use);  // 1 when not rebasing, 0 on the first tile
-        l = l * alpha + tsum;
-        m = m_use;
-        if (j > 0) {
-            // PV(j-1) reads P and accumulates into O: it must be done before P is
-            // overwritten and before O is rebased.
-            ok = warp_wait(b.o_done(w), (j - 1) & 1, abort_flag, kSiteODone);
-            if (!ok) break;
+        if (n == 0) continue;
+        stash[0] = item;
+        stash[1] = it;
+        float m = -INFINITY;  // exponent base: scaled row max, log2 domain (stale by < 8)
+        float l = 0.0f;       // running sum of 2^(x - m)
+        // One K tile.  The first of an item has no PV to wait for and no O to
+        // rescale; it is issued apart (`first` is a compile-time flag), so the
+        // loop over the other tiles carries no first-tile branch.  With the tile
+        // loop nested in the item loop, this peeling is worth about 6% per tile
+        // (measured at d=64).
+        auto tile = [&](int j, auto first) -> bool {
+            if (!warp_wait(b.s_full(w), (ph + j) & 1, abort_flag, kSiteSFull)) return false;
             tc_fence_after();
-            if (__any_sync(0xffffffffu, need)) {
-                float o[D];
-                load_cols<D>(tO, o);
+            float x[kBlockN];
+            {
+                uint32_t sr[kBlockN];
+                tmem_ld_x128_wait(tS, sr);
 #pragma unroll
-                for (int c = 0; c < D; ++c) o[c] *= alpha;
-                store_cols<D>(tO, o);
+                for (int c = 0; c < kBlockN; ++c) x[c] = __uint_as_float(sr[c]);
             }
-        }
-        tmem_st_x64(tP, pk);
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(b.p_full(w));
-    }
-
-    if (ok && n > 0) {
-        ok = warp_wait(b.o_done(w), (n - 1) & 1, abort_flag, kSiteODone);
-        if (ok) {
-            tc_fence_after();
-            float o[D];
-            load_cols<D>(tO, o);
-            if (row < seq_len) {
-                if (p.num_splits > 1) {
-                    write_partial<D>(p, wk, row, o, m, l);
-                } else {
-                    write_o_global<D>(p, wk, row, o, l);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(b.s_free(w));  // S may be overwritten by the next QK^T
+            const int jg = kv0 + j;  // K tile index in the sequence
+            prep_scores<0>(x, pre_scale, p.scale_log2, jg == diag, lim_of(p, row, jg));
+            prep_scores<1>(x, pre_scale, p.scale_log2, jg == diag, lim_of(p, row, jg));
+            const float m_new = fmaxf(m, row_max(x) * kmul);
+            const bool need = m_new > m + kRescaleThreshold;
+            float m_use = need ? m_new : m;
+            m_use = m_use == -INFINITY ? 0.0f : m_use;  // row with nothing visible yet
+            uint32_t pk[kBlockN / 2];
+            const float tsum = exp_row<kBf16>(x, kmul, m_use, pk);
+            const float alpha = ex2_approx(m - m_use);  // 1 when not rescaling, 0 on the first tile
+            l = l * alpha + tsum;
+            m = m_use;
+            if constexpr (!decltype(first)::value) {
+                // PV(j-1) reads P and accumulates into O: it must be done before P is
+                // overwritten and before O is rebased.  (At j = 0 the previous
+                // item's epilogue already waited for its last PV.)
+                if (!warp_wait(b.o_done(w), (ph + j - 1) & 1, abort_flag, kSiteODone)) return false;
+                tc_fence_after();
+                if (__any_sync(0xffffffffu, need)) {
+                    float o[D];
+                    load_cols<D>(tO, o);
+#pragma unroll
+                    for (int c = 0; c < D; ++c) o[c] *= alpha;
+                    store_cols<D>(tO, o);
                 }
             }
+            tmem_st_x64(tP, pk);
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(b.p_full(w));
+            return true;
+        };
+        ok = tile(0, std::true_type{});
+        for (int j = 1; ok && j < n; ++j) ok = tile(j, std::false_type{});
+        if (!ok) break;
+        // Epilogue: the item's last PV done, O read, O released to the next item's
+        // first PV, then written out.
+        ok = warp_wait(b.o_done(w), (ph + n - 1) & 1, abort_flag, kSiteODone);
+        if (!ok) break;
+        item = stash[0];
+        it = stash[1];
+        const Work wk = make_work(p, item);
+        tc_fence_after();
+        float o[D];
+        load_cols<D>(tO, o);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(b.o_free(w));
+        if (row < seq_len) {
+            if (p.num_splits > 1) {
+                write_partial<D>(p, wk, row, o, m, l);
+            } else {
+                write_o_global<D>(p, wk, row, o, l);
+            }
         }
+        ph ^= static_cast<uint32_t>(n) & 1u;
     }
 }
 
@@ -710,12 +859,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t *smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
     const uint32_t sbase = smem_u32(smem);
     const int warp = static_cast<int>(threadIdx.x >> 5), lane = static_cast<int>(threadIdx.x & 31);
-    const Work wk = make_work(p);
     volatile uint32_t *abort_flag = reinterpret_cast<volatile uint32_t *>(smem + L::kOffAbort);
     const Bars<D> b{sbase};
 
     if (threadIdx.x == 0) {
-        mbar_init(b.q_full(), 1);
+        for (int q = 0; q < 2; ++q) {
+            mbar_init(b.q_full(q), 1);
+            mbar_init(b.q_empty(q), kQTiles);  // one arrival per MMA warp and item
+        }
         for (int s = 0; s < L::kStages; ++s) {
             mbar_init(b.k_full(s), 1);
             mbar_init(b.v_full(s), 1);
@@ -726,21 +877,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(b.s_free(w), 4);  // one arrival per softmax warp
             mbar_init(b.p_full(w), 4);
             mbar_init(b.o_done(w), 1);
+            mbar_init(b.o_free(w), 4);
             mbar_init(b.drain(w), 1);
         }
-        for (int i = 0; i < 4 * kQTiles; ++i) mbar_init(b.at(L::kBarTurn + i), 1);
+        for (int c = 0; c < kClcSlots; ++c) {
+            mbar_init(b.clc_full(c), 1);
+            mbar_init(b.clc_empty(c), kClcReaders);  // one arrival per reader warp
+        }
         *abort_flag = 0u;
         mbar_fence_init();
     }
-    int issued = 0;
-    if (kTma && warp == 0) {
-        __syncwarp();  // barrier initialisation (thread 0) is visible to the warp
-        if (lane == 0) {
-            tma_prefetch_map(&tmap_q);
-            tma_prefetch_map(&tmap_k);
-            tma_prefetch_map(&tmap_v);
-        }
-        issued = producer_tma_prologue<D>(&tmap_q, &tmap_k, &tmap_v, sbase, wk);
+    if (kTma && warp == 0 && lane == 0) {
+        tma_prefetch_map(&tmap_q);
+        tma_prefetch_map(&tmap_k);
+        tma_prefetch_map(&tmap_v);
     }
     if (warp == 1) {
         tmem_alloc(sbase + L::kOffTmemSlot, kTmemCols);
@@ -753,15 +903,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == 0) {
         if constexpr (kTma) {
-            producer_tma<D>(&tmap_k, &tmap_v, sbase, wk, issued, abort_flag);
+            producer_tma<D>(p, &tmap_q, &tmap_k, &tmap_v, sbase, abort_flag, lane);
         } else {
-            producer_lsu<D>(p, smem, sbase, wk, abort_flag, lane);
+            producer_lsu<D>(p, smem, sbase, abort_flag, lane);
         }
         __syncwarp();
     } else if (warp == 1 || warp == 2) {
-        mma_role<D, kBf16>(warp - 1, sbase, tmem, wk, abort_flag, lane);
+        mma_role<D, kBf16>(p, warp - 1, sbase, tmem, abort_flag, lane);
     } else if (warp >= 4) {
-        softmax_role<D, kBf16>(p, sbase, tmem, wk, abort_flag, warp, lane);
+        softmax_role<D, kBf16>(p, smem, sbase, tmem, abort_flag, warp, lane);
     }
 
     tc_fence_before();

@@ -1,7 +1,7 @@
 // sm100_ptx.cuh -- hand-written PTX wrappers for the sm_100a primitives used by
-// the flash-attention forward kernel: mbarriers, TMA tensor loads, the
-// tcgen05 family (TMEM alloc/dealloc, MMA, commit, ld/st, fences) and the
-// UMMA descriptor builders.  Everything here is device code for sm_100a only.
+// the flash-attention forward kernel: mbarriers, TMA tensor loads, cluster
+// launch control, the tcgen05 family (TMEM alloc/dealloc, MMA, commit, ld/st,
+// fences) and the UMMA descriptor builders.  Everything here is device code for sm_100a only.
 //
 // Descriptor encodings (PTX ISA, tcgen05 "shared memory descriptor" and
 // "instruction descriptor" tables):
@@ -122,10 +122,47 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap *map
         ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z)
         : "memory");
 }
-// Orders this thread's generic-proxy shared-memory writes before later
-// async-proxy (tensor core) reads.
+// Orders this thread's generic-proxy shared-memory accesses before later
+// async-proxy (tensor core, TMA, launch-control) accesses.
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// --------------------------------------------------------------------------
+// Cluster launch control (sm_100): cancel a CTA of this grid that has not
+// started yet and take over its work.  The 16-byte response is written to
+// shared memory `resp` (16-byte aligned) and completes 16 bytes of
+// transaction on `bar`; one elected lane arms the barrier and issues the
+// request.  Single-CTA form (no multicast).
+// --------------------------------------------------------------------------
+__device__ __forceinline__ void clc_try_cancel_elect(uint32_t resp, uint32_t bar) {
+    asm volatile(
+        "{\n"
+        ".reg .pred e;\n"
+        "elect.sync _|e, -1;\n"
+        "@e mbarrier.arrive.expect_tx.shared::cta.b64 _, [%1], 16;\n"
+        "@e clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes.b128 [%0], [%1];\n"
+        "}\n" ::"r"(resp),
+        "r"(bar)
+        : "memory");
+}
+// blockIdx.x of the CTA a response cancelled, or -1 when the request found
+// no CTA left to cancel.
+__device__ __forceinline__ int clc_decode(uint32_t resp) {
+    uint32_t x = 0, valid;
+    asm volatile(
+        "{\n"
+        ".reg .pred p;\n"
+        ".reg .b128 r;\n"
+        "ld.shared.b128 r, [%2];\n"
+        "clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p, r;\n"
+        "selp.u32 %1, 1, 0, p;\n"
+        "@p clusterlaunchcontrol.query_cancel.get_first_ctaid::x.b32.b128 %0, r;\n"
+        "}\n"
+        : "+r"(x), "=r"(valid)
+        : "r"(resp)
+        : "memory");
+    return valid ? static_cast<int>(x) : -1;
 }
 
 // --------------------------------------------------------------------------

@@ -506,3 +506,26 @@ def test_bf16_output_from_f16_inputs(ncz, oracle_mod):
     p = C.normal_problem(2, 300, 32, False, 37, oracle_mod, std=0.7)
     got = run(ncz, p, o_dtype="bfloat16")
     C.check(got, C.reference(p, oracle_mod), C.active_index(p), "f16 in, bf16 out", atol=C.ATOL_BF16)
+
+
+def test_many_items_per_cta_with_empty_q_tiles(ncz, oracle_mod):
+    """bh=300, S=600, causal: 900 work items, one resident CTA per SM taking
+    further items through launch control (Q double-buffered across them,
+    pipelines swapping Q tiles per item), and every slice's last item has an
+    empty second Q tile (rows 640.. >= S); all rows against the oracle."""
+    p = C.normal_problem(300, 600, 32, True, 71, oracle_mod, std=0.8)
+    got = run(ncz, p)
+    idx = C.active_index(p)
+    C.check(got, C.reference(p, oracle_mod), idx, "bh=300 S=600 causal (item walk)")
+    assert untouched(got, p, idx)
+
+
+def test_item_walk_split_kv_with_empty_ranges(ncz, oracle_mod):
+    """bh=2, S=8192, causal, 8 forced splits: 512 items, most early groups' later
+    K ranges empty (items without work taken and passed on); two slices' head
+    and tail rows against the oracle."""
+    p = C.normal_problem(2, 8192, 64, True, 73, oracle_mod, std=0.7)
+    got = run(ncz, p, splits=8)
+    for rows in ((0, 300), (7900, 8192)):
+        idx = C.active_index(p, rows=rows)
+        C.check(got, C.reference(p, oracle_mod, rows=rows), idx, f"split 8 rows {rows}")
