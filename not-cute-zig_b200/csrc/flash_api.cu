@@ -34,6 +34,11 @@ constexpr size_t kGroupRows = static_cast<size_t>(ncz::kBlockM) * ncz::kQTiles; 
 constexpr int kVariants = 12;  // (D in 16/32/64) x (TMA, LSU) x (f16, bf16 inputs)
 // Items with at least this many K tiles end their CTA instead of taking the
 // next item; measured fastest with every item taking the next one.
+// K/V bytes per chunk of slices in the item order (measured best of 16-96 MB
+// at d=64: 32 MB, e.g. 16 slices at S=8192).
+#ifndef NCZ_CHUNK_KV_BYTES
+#define NCZ_CHUNK_KV_BYTES (32u << 20)
+#endif
 #ifndef NCZ_WALK_TILES
 #define NCZ_WALK_TILES (1 << 30)
 #endif
@@ -395,6 +400,13 @@ int launch_on_current(const Resolved &r, int dev) {
     const size_t items = static_cast<size_t>(p.num_groups) * r.bh * static_cast<size_t>(p.num_splits);
     const unsigned grid = static_cast<unsigned>(items);
     p.walk_tiles = NCZ_WALK_TILES;
+    {
+        // NCZ_CHUNK_KV_BYTES of K/V per chunk of slices: with the items in
+        // flight spanning at most two chunks, the K/V being read stays in L2.
+        const size_t kv_slice = static_cast<size_t>(r.seq) * r.d * 2 * 2;
+        const size_t c = std::max<size_t>(1, (NCZ_CHUNK_KV_BYTES) / std::max<size_t>(kv_slice, 1));
+        p.chunk_slices = static_cast<int>(std::min<size_t>(c, r.bh));
+    }
     const bool bf = r.in_dtype == NCZ_DTYPE_BF16;
     int st;
     switch (r.d) {

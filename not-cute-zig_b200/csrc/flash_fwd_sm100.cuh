@@ -127,6 +127,10 @@ struct FlashParams {
     // A CTA takes a further item (launch control) only while its current item
     // has fewer than walk_tiles K tiles; heavier items end their CTA.
     int walk_tiles;
+    // Items run in chunks of chunk_slices slices (all of a chunk's groups,
+    // heaviest first, before the next chunk), so the K/V a chunk reads stays in
+    // L2 while its groups pass over it.
+    int chunk_slices;
     float *part_o;
     float *part_ml;
 };
@@ -190,11 +194,18 @@ __device__ int g_ncz_test_drop = 0;
 
 __device__ __forceinline__ Work make_work(const FlashParams &p, int item) {
     Work wk;
-    // Heaviest (last) Q-tile groups first: under causal masking they visit the most K tiles.
-    const int per_group = p.batch_heads * p.num_splits;
-    const int group = p.num_groups - 1 - item / per_group;
-    const int rem = item % per_group;
-    wk.slice = rem / p.num_splits;
+    // Chunks of chunk_slices slices; inside a chunk the heaviest (last) Q-tile
+    // groups first (under causal masking they visit the most K tiles), then
+    // slice, then K range.
+    const int per_chunk = p.chunk_slices * p.num_groups * p.num_splits;
+    const int chunk = item / per_chunk;
+    const int off = item - chunk * per_chunk;
+    const int c0 = chunk * p.chunk_slices;
+    const int slices = min(p.chunk_slices, p.batch_heads - c0);  // the last chunk may be short
+    const int per_group = slices * p.num_splits;
+    const int group = p.num_groups - 1 - off / per_group;
+    const int rem = off % per_group;
+    wk.slice = c0 + rem / p.num_splits;
     wk.split = rem % p.num_splits;
     wk.q_base = group * (kQTiles * kBlockM);
     wk.kv0 = wk.split * p.kv_per_split;

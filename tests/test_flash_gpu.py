@@ -529,3 +529,16 @@ def test_item_walk_split_kv_with_empty_ranges(ncz, oracle_mod):
     for rows in ((0, 300), (7900, 8192)):
         idx = C.active_index(p, rows=rows)
         C.check(got, C.reference(p, oracle_mod, rows=rows), idx, f"split 8 rows {rows}")
+
+
+def test_item_order_chunks_with_short_last_chunk(ncz, oracle_mod):
+    """bh=20, S=8192, d=64, causal: 2 MB of K/V per slice, so the item order runs
+    a chunk of 16 slices, then a short chunk of 4; head, middle and tail rows of
+    slices on both sides of the chunk edge against the oracle."""
+    p = C.normal_problem(20, 8192, 64, True, 79, oracle_mod, std=0.7)
+    got = run(ncz, p)
+    sl = [0, 15, 16, 19]
+    for rows in ((0, 130), (4000, 4100), (8100, 8192)):
+        idx = C.active_index(p, slices=sl, rows=rows)
+        want = C.reference(p, oracle_mod, slices=sl, rows=rows)
+        C.check(got, want, idx, f"chunked order rows {rows}")
