@@ -63,6 +63,15 @@ constexpr int kThreads = 128 * (1 + kQTiles);
 // Launch-control response ring (next work items) and the warps that read each
 // response: the producer, the MMA warps and the softmax warps.
 constexpr int kClcSlots = 4;
+// The producer asks for the next item once it has a ring slot for the item's
+// kClcLead-th last K/V tile: late enough that a CTA does not hold on to an
+// item it will start only much later (which stretched the end of a launch
+// whose last items differ in size), early enough that the answer is back
+// before the next item's loads are due.
+#ifndef NCZ_CLC_LEAD
+#define NCZ_CLC_LEAD 1
+#endif
+constexpr int kClcLead = NCZ_CLC_LEAD;
 constexpr uint32_t kClcReaders = 1 + kQTiles + 4 * kQTiles;
 constexpr uint32_t kTmemCols = 512;
 // TMEM column map per Q tile w (base kTileCols * w): S | P | O
@@ -349,18 +358,19 @@ __device__ __forceinline__ void producer_tma(const FlashParams &p, const CUtenso
                                   wk.q_base + w * kBlockM, wk.slice);
         const int cur = it++;
         const bool walk = wk.n_max < p.walk_tiles;
-        if (walk) {
-            if (!request_item(b, cur, abort_flag)) {
-                ok = false;
-                break;
-            }
-            pending = cur;
-        }
+        const int req_at = wk.n_max > kClcLead ? wk.n_max - kClcLead : 0;  // see kClcLead
         for (int j = 0; j < wk.n_max; ++j, ++t) {
             const int st = t % L::kStages;
             if (t >= L::kStages && !warp_wait(b.kv_empty(st), ((t / L::kStages) - 1) & 1, abort_flag, kSiteKvEmpty)) {
                 ok = false;
                 break;
+            }
+            if (walk && j == req_at) {
+                if (!request_item(b, cur, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                pending = cur;
             }
             mbar_arrive_expect_tx_elect(b.k_full(st), L::kKvTile);
             tma_load_3d_elect(sbase + L::kOffK + st * L::kKvTile, tk, b.k_full(st), 0, (wk.kv0 + j) * kBlockN,
@@ -370,6 +380,10 @@ __device__ __forceinline__ void producer_tma(const FlashParams &p, const CUtenso
                               wk.slice);
         }
         if (!ok) break;
+        if (walk && wk.n_max == 0) {  // no K tiles: ask now
+            if (!request_item(b, cur, abort_flag)) break;
+            pending = cur;
+        }
         item = walk ? take_item(b, it, abort_flag, lane) : -1;
         if (item != -2) pending = -1;
     }
@@ -432,10 +446,7 @@ __device__ __forceinline__ void producer_lsu(const FlashParams &p, uint8_t *smem
         if (it >= 2 && !warp_wait(b.q_empty(slot), ((it >> 1) - 1) & 1, abort_flag, kSiteQEmpty)) break;
         const int cur = it++;
         const bool walk = wk.n_max < p.walk_tiles;
-        if (walk) {
-            if (!request_item(b, cur, abort_flag)) break;
-            pending = cur;
-        }
+        const int req_at = wk.n_max > kClcLead ? wk.n_max - kClcLead : 0;  // see kClcLead
 #pragma unroll
         for (int w = 0; w < kQTiles; ++w)
             if (wk.n[w] > 0)
@@ -450,6 +461,13 @@ __device__ __forceinline__ void producer_lsu(const FlashParams &p, uint8_t *smem
                 ok = false;
                 break;
             }
+            if (walk && j == req_at) {
+                if (!request_item(b, cur, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                pending = cur;
+            }
             lsu_tile<D, kBlockN>(smem + L::kOffK + st * L::kKvTile, ks, p.k_row, (wk.kv0 + j) * kBlockN, p.seq_len,
                                  lane);
             fence_proxy_async_smem();
@@ -462,6 +480,10 @@ __device__ __forceinline__ void producer_lsu(const FlashParams &p, uint8_t *smem
             if (lane == 0) mbar_arrive(b.v_full(st));
         }
         if (!ok) break;
+        if (walk && wk.n_max == 0) {  // no K tiles: ask now
+            if (!request_item(b, cur, abort_flag)) break;
+            pending = cur;
+        }
         item = walk ? take_item(b, it, abort_flag, lane) : -1;
         if (item != -2) pending = -1;
     }
