@@ -699,14 +699,16 @@ __device__ __forceinline__ void write_partial(const FlashParams &p, const Work &
     *reinterpret_cast<float2 *>(p.part_ml + idx * 2) = make_float2(m, l);
 }
 
-// Row max of kBlockN scores with 8 independent chains: chain i covers x[i], x[8+i], ...
+// Row max of the first kCols of kBlockN scores with 8 independent chains:
+// chain i covers x[i], x[8+i], ...
+template <int kCols = kBlockN>
 __device__ __forceinline__ float row_max(const float (&x)[kBlockN]) {
-    static_assert(kBlockN % 16 == 0, "tile width");
+    static_assert(kCols % 16 == 0 && kCols <= kBlockN, "tile width");
     float mx[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) mx[i] = fmaxf(x[i], x[8 + i]);
 #pragma unroll
-    for (int c = 16; c + 16 <= kBlockN; c += 16) {
+    for (int c = 16; c + 16 <= kCols; c += 16) {
 #pragma unroll
         for (int i = 0; i < 8; ++i) mx[i] = fmax3(mx[i], x[c + i], x[c + 8 + i]);
     }
@@ -716,13 +718,16 @@ __device__ __forceinline__ float row_max(const float (&x)[kBlockN]) {
 // Exponentiates one score row in place against base m (log2 domain), packs P
 // to pairs of the input type (f16 as src/flash_h64_bn32.zig:185, or bf16: the
 // PV MMA takes A and B of one type) and sums the unrounded values in four
-// independent chains.
-template <bool kBf16>
+// independent chains.  Only the first kCols scores are exponentiated; P of the
+// others is 0 (all of them masked).
+template <bool kBf16, int kCols = kBlockN>
 __device__ __forceinline__ float exp_row(float (&x)[kBlockN], float kmul, float m, uint32_t (&pk)[kBlockN / 2]) {
     const uint64_t kmul2 = pack_f32x2(kmul, kmul), negm2 = pack_f32x2(-m, -m);
     uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};  // (0.0f, 0.0f) x 4
 #pragma unroll
-    for (int c = 0; c < kBlockN / 2; ++c) {
+    for (int c = kCols / 2; c < kBlockN / 2; ++c) pk[c] = 0u;  // +0 in f16 and bf16
+#pragma unroll
+    for (int c = 0; c < kCols / 2; ++c) {
         float e0, e1, p0, p1;
         unpack_f32x2(ffma2(pack_f32x2(x[2 * c], x[2 * c + 1]), kmul2, negm2), e0, e1);
         if (kExp2EmuPeriod > 0 && c % kExp2EmuPeriod >= kExp2EmuPeriod - kExp2EmuCount) {
@@ -802,11 +807,12 @@ __device__ __forceinline__ void softmax_role(const FlashParams &p, uint8_t *smem
         float m = -INFINITY;  // exponent base: scaled row max, log2 domain (stale by < 8)
         float l = 0.0f;       // running sum of 2^(x - m)
         // One K tile.  The first of an item has no PV to wait for and no O to
-        // rescale; it is issued apart (`first` is a compile-time flag), so the
-        // loop over the other tiles carries no first-tile branch.  With the tile
-        // loop nested in the item loop, this peeling is worth about 6% per tile
-        // (measured at d=64).
-        auto tile = [&](int j, auto first) -> bool {
+        // rescale, and only the last can hold masked keys (K tile index diag,
+        // or a ragged end); both are issued apart (`first` and `final` are
+        // compile-time flags), so the loop over the other tiles carries neither
+        // branch.  With the tile loop nested in the item loop, peeling the first
+        // tile is worth about 6% per tile (measured at d=64).
+        auto tile = [&](int j, auto first, auto final) -> bool {
             if (!warp_wait(b.s_full(w), (ph + j) & 1, abort_flag, kSiteSFull)) return false;
             tc_fence_after();
             float x[kBlockN];
@@ -819,15 +825,34 @@ __device__ __forceinline__ void softmax_role(const FlashParams &p, uint8_t *smem
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(b.s_free(w));  // S may be overwritten by the next QK^T
-            const int jg = kv0 + j;  // K tile index in the sequence
-            prep_scores<0>(x, pre_scale, p.scale_log2, jg == diag, lim_of(p, row, jg));
-            prep_scores<1>(x, pre_scale, p.scale_log2, jg == diag, lim_of(p, row, jg));
-            const float m_new = fmaxf(m, row_max(x) * kmul);
+            bool half = false;
+            float mx;
+            if constexpr (decltype(final)::value) {
+                const int jg = kv0 + j;  // K tile index in the sequence
+                const bool last = jg == diag;
+                const int lim = lim_of(p, row, jg);
+                // Every key of the upper half masked for all 32 rows of this warp
+                // (rows 0-63 of a Q tile on the causal diagonal): only the lower
+                // half is exponentiated.
+                half = last && __all_sync(0xffffffffu, lim <= kBlockN / 2);
+                prep_scores<0>(x, pre_scale, p.scale_log2, last, lim);
+                if (half) {
+                    mx = row_max<kBlockN / 2>(x);
+                } else {
+                    prep_scores<1>(x, pre_scale, p.scale_log2, last, lim);
+                    mx = row_max(x);
+                }
+            } else {
+                prep_scores<0>(x, pre_scale, p.scale_log2, false, kBlockN);
+                prep_scores<1>(x, pre_scale, p.scale_log2, false, kBlockN);
+                mx = row_max(x);
+            }
+            const float m_new = fmaxf(m, mx * kmul);
             const bool need = m_new > m + kRescaleThreshold;
             float m_use = need ? m_new : m;
             m_use = m_use == -INFINITY ? 0.0f : m_use;  // row with nothing visible yet
             uint32_t pk[kBlockN / 2];
-            const float tsum = exp_row<kBf16>(x, kmul, m_use, pk);
+            const float tsum = half ? exp_row<kBf16, kBlockN / 2>(x, kmul, m_use, pk) : exp_row<kBf16>(x, kmul, m_use, pk);
             const float alpha = ex2_approx(m - m_use);  // 1 when not rescaling, 0 on the first tile
             l = l * alpha + tsum;
             m = m_use;
@@ -838,11 +863,18 @@ __device__ __forceinline__ void softmax_role(const FlashParams &p, uint8_t *smem
                 if (!warp_wait(b.o_done(w), (ph + j - 1) & 1, abort_flag, kSiteODone)) return false;
                 tc_fence_after();
                 if (__any_sync(0xffffffffu, need)) {
-                    float o[D];
-                    load_cols<D>(tO, o);
+                    // In chunks of at most 32 columns: fewer registers on this
+                    // (rare) path, next to the 64 of P.
+                    constexpr int kC = D < 32 ? D : 32;
 #pragma unroll
-                    for (int c = 0; c < D; ++c) o[c] *= alpha;
-                    store_cols<D>(tO, o);
+                    for (int c0 = 0; c0 < D; c0 += kC) {
+                        float o[kC];
+                        load_cols<kC>(tO + c0, o);
+#pragma unroll
+                        for (int c = 0; c < kC; ++c) o[c] *= alpha;
+                        store_cols<kC>(tO + c0, o);
+                        tmem_wait_st();
+                    }
                 }
             }
             tmem_st_x64(tP, pk);
@@ -852,8 +884,13 @@ __device__ __forceinline__ void softmax_role(const FlashParams &p, uint8_t *smem
             if (lane == 0) mbar_arrive(b.p_full(w));
             return true;
         };
-        ok = tile(0, std::true_type{});
-        for (int j = 1; ok && j < n; ++j) ok = tile(j, std::false_type{});
+        if (n == 1) {
+            ok = tile(0, std::true_type{}, std::true_type{});
+        } else {
+            ok = tile(0, std::true_type{}, std::false_type{});
+            for (int j = 1; ok && j + 1 < n; ++j) ok = tile(j, std::false_type{}, std::false_type{});
+            if (ok) ok = tile(n - 1, std::false_type{}, std::true_type{});
+        }
         if (!ok) break;
         // Epilogue: the item's last PV done, O read, O released to the next item's
         // first PV, then written out.
