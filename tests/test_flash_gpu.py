@@ -542,3 +542,14 @@ def test_item_order_chunks_with_short_last_chunk(ncz, oracle_mod):
         idx = C.active_index(p, slices=sl, rows=rows)
         want = C.reference(p, oracle_mod, slices=sl, rows=rows)
         C.check(got, want, idx, f"chunked order rows {rows}")
+
+
+def test_item_walk_lsu_equals_tma(ncz, oracle_mod):
+    """bh=300, S=600, d=32, causal: 900 items walked through launch control with
+    each producer (TMA, and plain loads that request the next item the same
+    way); bit-identical outputs, against the oracle."""
+    p = C.normal_problem(300, 600, 32, True, 83, oracle_mod, std=0.8)
+    a = run(ncz, p, producer="tma")
+    b = run(ncz, p, producer="lsu")
+    C.check(a, C.reference(p, oracle_mod), C.active_index(p), "item walk, TMA producer")
+    assert np.array_equal(a, b)
