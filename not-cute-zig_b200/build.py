@@ -1,4 +1,5 @@
-"""Build recipe for libncz_flash.so (sm_100a only), in-tree.
+"""Build recipe for libncz_flash.so (sm_100a only), in-tree: the flash-attention
+forward (csrc/flash_api.cu) and the batched GEMM with epilogue (csrc/mma_api.cu).
 
 nvcc -gencode arch=compute_100a,code=sm_100a -O3 -lineinfo -shared -fPIC,
 static cudart (the library resolves cuTensorMapEncodeTiled at run time, so
@@ -20,7 +21,7 @@ FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17", "-li
 
 
 def sources():
-    return [os.path.join(HERE, "csrc", "flash_api.cu")]
+    return [os.path.join(HERE, "csrc", "flash_api.cu"), os.path.join(HERE, "csrc", "mma_api.cu")]
 
 
 def deps():

@@ -12,6 +12,7 @@ src/main.zig:1042); rel = |a - b| / max(|b|, 1e-3).
 
     python not-cute-zig_b200/compare.py                  # the 15 reference shapes
     python not-cute-zig_b200/compare.py --shape 8,1024,64,1 --gpus 2 --jsonl out.jsonl
+    python not-cute-zig_b200/compare.py --mma        # GEMM + epilogue (compareMma, src/main.zig:953-975)
 """
 from __future__ import annotations
 
@@ -121,15 +122,95 @@ def compare_shape(ncz, bh: int, s: int, d: int, causal: bool, gpus: int = 1) -> 
                       max_rel_error=max_rel, host_cores=bench.host_cores(), label=label)
 
 
+def measured_hbm() -> Optional[float]:
+    path = os.path.join(os.path.dirname(_HERE), "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"])
+    except (OSError, KeyError, ValueError):
+        return None
+
+
+def torch_gemm(a, b, c, batches: int, k_iters: int, alpha: float, beta: float, epilogue: int, b_col: bool):
+    """fp32 D = act(alpha * A B + beta * C) per batch in torch (cross-check
+    only), the activations written as src/device.zig:57-80 writes them (exp2
+    forms; silu and gelu give NaN where exp2 overflows, as there)."""
+    import torch
+
+    am = a.view(batches, k_iters, 16, 16).float().permute(0, 2, 1, 3).reshape(batches, 16, 16 * k_iters)
+    if b_col:
+        bm = b.view(batches, k_iters, 8, 16).float().transpose(2, 3).reshape(batches, 16 * k_iters, 8)
+    else:
+        bm = b.view(batches, k_iters, 16, 8).float().reshape(batches, 16 * k_iters, 8)
+    out = alpha * torch.bmm(am, bm) + beta * c.view(batches, 16, 8)
+    log2e = 1.4426950408889634
+    if epilogue == 1:
+        out = torch.relu(out)
+    elif epilogue == 2:
+        e = torch.exp2(out * log2e)
+        out = out * (e / (1.0 + e))
+    elif epilogue == 3:
+        e = torch.exp2(2.0 * (0.7978845608 * (out + 0.044715 * out * out * out)) * log2e)
+        out = 0.5 * out * (1.0 + (e - 1.0) / (e + 1.0))
+    return out.reshape(-1)
+
+
+def compare_mma(ncz, batches: int, k_iters: int, epilogue: int) -> dict:
+    """compareMma (src/main.zig:953-975) for batches = k_iters = 1 (mma_matmul,
+    16x8x16, alpha 1, beta 0); otherwise pipelined_mma_matmul over `batches`
+    batches (the reference runs one): 5 warm-up + 20 timed launches,
+    algorithmic bytes = A, B f16 read + C f32 read + D f32 written."""
+    import torch
+
+    bench = importlib.import_module("not-cute-zig_b200.benchmark")
+    single = batches == 1 and k_iters == 1
+    g = torch.Generator(device="cuda")
+    g.manual_seed(batches * 31 + k_iters)
+    a = (torch.rand(batches * k_iters * 256, generator=g, device="cuda") * 2 - 1).half()
+    b = (torch.rand(batches * k_iters * 128, generator=g, device="cuda") * 2 - 1).half()
+    c = torch.rand(batches * 128, generator=g, device="cuda") * 2 - 1
+    d = torch.empty_like(c)
+    alpha, beta = (1.0, 0.0) if single else (1.0, 0.5)
+    stream = torch.cuda.current_stream()
+    if single:
+        launch = lambda: ncz.mma.mma_matmul(a, b, c, d, alpha, beta, stream=stream)  # noqa: E731
+    else:
+        launch = lambda: ncz.mma.pipelined_mma_matmul(a, b, c, d, alpha, beta, k_iters * 256, k_iters * 128,  # noqa: E731
+                                                      128, k_iters, epilogue, batches, stream=stream)
+    bytes_ = ncz.mma.bytes_moved(k_iters, batches)
+    flops = ncz.mma.flops(k_iters, batches)
+    res = bench.run_kernel(launch, warmup_iters=5, iters=20, bytes_processed=bytes_, flops_processed=flops,
+                           stream=stream)
+    ncz.mma.sync_status()
+    want = torch_gemm(a, b, c, batches, k_iters, alpha, beta, 0 if single else epilogue, single)
+    nan_match = bool(torch.equal(torch.isnan(d), torch.isnan(want)))
+    ok = ~torch.isnan(want)
+    err = float((d[ok] - want[ok]).abs().max()) if nan_match else float("nan")
+    peak = measured_hbm()
+    shape = "16x8x16" if single else f"batches={batches},k_iters={k_iters},16x8,epilogue={int(epilogue)}"
+    return res.record("mma_gemm", "not_cute_zig_b200", shape, nan_match and err <= 1e-3, bytes_, flops, err,
+                      pct_hbm_measured=(res.throughput_gbps / peak) if peak else None, host_cores=bench.host_cores(),
+                      label="mma_gemm_sm100a")
+
+
+MMA_SHAPES = [(1, 1, 0), (1 << 21, 1, 1), (1 << 20, 4, 2), (1 << 18, 16, 3)]
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--shape", action="append", default=[],
                     help="bh,seq,head,causal (repeatable); default: the 15 reference compare shapes")
     ap.add_argument("--gpus", type=int, default=1, help="shard slices across this many devices")
     ap.add_argument("--jsonl", default=None, help="append records to this file instead of stdout")
+    ap.add_argument("--mma", action="store_true",
+                    help="the GEMM + epilogue records instead: compareMma's 16x8x16 and batched throughput shapes")
     args = ap.parse_args(argv)
     ncz = importlib.import_module("not-cute-zig_b200")
     bench = importlib.import_module("not-cute-zig_b200.benchmark")
+    if args.mma:
+        records = [compare_mma(ncz, nb, k, e) for nb, k, e in MMA_SHAPES]
+        bench.emit(records, args.jsonl)
+        return 0 if all(r["correct"] for r in records) else 1
     shapes = REFERENCE_SHAPES
     if args.shape:
         shapes = []

@@ -22,6 +22,7 @@
 #include <vector>
 
 #include "flash_fwd_sm100.cuh"
+#include "status.cuh"
 #include "ncz_flash.h"
 
 namespace {
@@ -50,28 +51,7 @@ PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::atomic<uint64_t> g_launches{0};
 bool g_attr_done[kMaxDevices][kVariants];
 
-int map_cuda_error(cudaError_t e) {
-    switch (e) {
-        case cudaSuccess: return NCZ_SUCCESS;
-        case cudaErrorMemoryAllocation: return NCZ_ERROR_OUT_OF_MEMORY;
-        case cudaErrorSharedObjectInitFailed: return NCZ_ERROR_SHARED_OBJECT_INIT_FAILED;
-        case cudaErrorSymbolNotFound: return NCZ_ERROR_NOT_FOUND;
-        case cudaErrorInvalidValue: return NCZ_ERROR_INVALID_VALUE;
-        case cudaErrorDeviceUninitialized: return NCZ_ERROR_INVALID_CONTEXT;
-        case cudaErrorInvalidDevice: return NCZ_ERROR_INVALID_DEVICE;
-        case cudaErrorInvalidKernelImage:
-        case cudaErrorNoKernelImageForDevice: return NCZ_ERROR_INVALID_IMAGE;
-        case cudaErrorContextIsDestroyed: return NCZ_ERROR_CONTEXT_IS_DESTROYED;
-        case cudaErrorLaunchFailure: return NCZ_ERROR_LAUNCH_FAILED;
-        case cudaErrorLaunchOutOfResources: return NCZ_ERROR_LAUNCH_OUT_OF_RESOURCES;
-        case cudaErrorLaunchTimeout: return NCZ_ERROR_LAUNCH_TIMEOUT;
-        case cudaErrorIllegalAddress: return NCZ_ERROR_ILLEGAL_ADDRESS;
-        case cudaErrorNoDevice: return NCZ_ERROR_NO_DEVICE;
-        case cudaErrorInitializationError:
-        case cudaErrorInsufficientDriver: return NCZ_ERROR_NOT_INITIALIZED;
-        default: return NCZ_ERROR_UNKNOWN;
-    }
-}
+using ncz::map_cuda_error;
 
 // Fully resolved launch description: row strides defaulted, dtype checked.
 struct Resolved {

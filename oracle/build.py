@@ -1,7 +1,8 @@
 """Build recipes for the test oracle (TEST INFRASTRUCTURE ONLY).
 
-- liboracle.so: the plain-C restatement of the reference CPU attention
-  (oracle/flash_oracle.c), gcc -O2 -fno-fast-math -fopenmp.
+- liboracle.so: the plain-C restatements of the reference CPU attention
+  (oracle/flash_oracle.c) and of its CPU GEMM references (oracle/mma_oracle.c),
+  gcc -O2 -fno-fast-math -fopenmp.
 - _ref/libncz_ref.so and _ref/cuda_baselines: the reference's own
   tools/cuda_baselines.cu compiled from where it lies in the reference tree
   (only when that tree is present); they travel to GPU boxes as built files.
@@ -32,10 +33,14 @@ def _stale(out, srcs):
     return any(os.path.getmtime(s) > t for s in srcs)
 
 
+def oracle_sources():
+    return [os.path.join(HERE, "flash_oracle.c"), os.path.join(HERE, "mma_oracle.c")]
+
+
 def build_oracle(force: bool = False) -> str:
-    src = os.path.join(HERE, "flash_oracle.c")
-    if force or _stale(ORACLE_SO, [src]):
-        _run(["gcc", "-O2", "-fno-fast-math", "-fopenmp", "-fPIC", "-shared", "-std=c11", src, "-o", ORACLE_SO,
+    srcs = oracle_sources()
+    if force or _stale(ORACLE_SO, srcs):
+        _run(["gcc", "-O2", "-fno-fast-math", "-fopenmp", "-fPIC", "-shared", "-std=c11"] + srcs + ["-o", ORACLE_SO,
               "-lm"])
     return ORACLE_SO
 

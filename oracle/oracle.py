@@ -20,9 +20,9 @@ _lib = None
 def lib() -> ctypes.CDLL:
     global _lib
     if _lib is None:
-        src = os.path.join(os.path.dirname(os.path.abspath(__file__)), "flash_oracle.c")
-        if not os.path.exists(_build.ORACLE_SO) or (
-                os.path.exists(src) and os.path.getmtime(src) > os.path.getmtime(_build.ORACLE_SO)):
+        srcs = [p for p in _build.oracle_sources() if os.path.exists(p)]
+        if not os.path.exists(_build.ORACLE_SO) or any(
+                os.path.getmtime(p) > os.path.getmtime(_build.ORACLE_SO) for p in srcs):
             _build.build_oracle()
         h = ctypes.CDLL(_build.ORACLE_SO)
         sz, vp = ctypes.c_size_t, ctypes.c_void_p
@@ -43,6 +43,9 @@ def lib() -> ctypes.CDLL:
         h.ncz_oracle_fill_row_padding.argtypes = [vp, sz, sz, sz, sz, sz, ctypes.c_uint16]
         h.ncz_oracle_max_threads.restype = ctypes.c_int
         h.ncz_oracle_max_threads.argtypes = []
+        h.ncz_oracle_mma.restype = None
+        h.ncz_oracle_mma.argtypes = [vp, vp, vp, vp, ctypes.c_float, ctypes.c_float, sz, sz, sz, sz, ctypes.c_uint32,
+                                     sz, ctypes.c_int]
         _lib = h
     return _lib
 
@@ -116,3 +119,20 @@ def bf16_to_f32(bits: np.ndarray) -> np.ndarray:
 
 def max_threads() -> int:
     return int(lib().ncz_oracle_max_threads())
+
+
+def mma_reference(a: np.ndarray, b: np.ndarray, c: np.ndarray, *, alpha: float, beta: float, batch_stride_a: int,
+                  batch_stride_b: int, batch_stride_c: int, k_iters: int, epilogue: int, batches: int,
+                  b_col: bool = False) -> np.ndarray:
+    """GEMM + epilogue oracle (mma_oracle.c: computePipelineReference,
+    src/main.zig:1184-1204, and computeMmaReference, :1146-1162, generalised
+    to batches, strides and the silu / gelu activations of src/device.zig).
+    Returns D as float32 with C's shape (entries outside the batches' tiles are
+    copied from C)."""
+    a = np.ascontiguousarray(a, dtype=np.float16)
+    b = np.ascontiguousarray(b, dtype=np.float16)
+    c = np.ascontiguousarray(c, dtype=np.float32)
+    d = c.copy()
+    lib().ncz_oracle_mma(_ptr(a), _ptr(b), _ptr(c), _ptr(d), alpha, beta, batch_stride_a, batch_stride_b,
+                         batch_stride_c, k_iters, epilogue, batches, 1 if b_col else 0)
+    return d

@@ -9,17 +9,19 @@ import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 HEADER = os.path.join(ROOT, "include", "ncz_flash.h")
+HEADERS = sorted(os.path.join(ROOT, "include", f) for f in os.listdir(os.path.join(ROOT, "include")) if f.endswith(".h"))
 
 
 def declared_functions():
-    text = open(HEADER).read()
+    text = "".join(open(h).read() for h in HEADERS)
     return sorted(set(re.findall(r"\b(ncz_[a-z0-9_]+)\s*\(", text)))
 
 
 def test_library_exports_every_declared_symbol(ncz):
     lib = ncz.flash.lib()
     names = declared_functions()
-    assert len(names) >= 15
+    assert len(names) >= 19
+    assert {"ncz_mma_matmul_pipelined", "ncz_mma_matmul_batched", "ncz_mma_matmul"} <= set(names)
     for name in names:
         assert hasattr(lib, name), name
     out = subprocess.run(["nm", "-D", "--defined-only", ncz.flash.LIB_PATH], capture_output=True, text=True).stdout
