@@ -204,11 +204,14 @@ def main(argv=None) -> int:
     ap.add_argument("--jsonl", default=None, help="append records to this file instead of stdout")
     ap.add_argument("--mma", action="store_true",
                     help="the GEMM + epilogue records instead: compareMma's 16x8x16 and batched throughput shapes")
+    ap.add_argument("--mma-shape", action="append", default=[],
+                    help="batches,k_iters,epilogue (repeatable; implies --mma)")
     args = ap.parse_args(argv)
     ncz = importlib.import_module("not-cute-zig_b200")
     bench = importlib.import_module("not-cute-zig_b200.benchmark")
-    if args.mma:
-        records = [compare_mma(ncz, nb, k, e) for nb, k, e in MMA_SHAPES]
+    if args.mma or args.mma_shape:
+        shapes = [tuple(int(x) for x in spec.split(",")) for spec in args.mma_shape] or MMA_SHAPES
+        records = [compare_mma(ncz, nb, k, e) for nb, k, e in shapes]
         bench.emit(records, args.jsonl)
         return 0 if all(r["correct"] for r in records) else 1
     shapes = REFERENCE_SHAPES
