@@ -56,6 +56,15 @@ int ncz_mma_matmul(const void *a, const void *b, const void *c, void *d, float a
  * cleanly; D is incomplete). */
 int ncz_mma_sync_status(int device);
 
+/* Test hooks (failure detection without a GPU fault), device -1 = current.
+ * ncz_mma_test_set_wait_limit: bound of every stage wait in SM cycles
+ * (0 restores the default of about 2 s).  ncz_mma_test_drop_copy: while
+ * enabled, the first warp of a launch arms its first stage for bytes it never
+ * copies, so that wait runs out and the next ncz_mma_sync_status reports
+ * NCZ_ERROR_DEVICE_TIMEOUT. */
+int ncz_mma_test_set_wait_limit(int device, uint64_t cycles);
+int ncz_mma_test_drop_copy(int device, int enable);
+
 #ifdef __cplusplus
 }
 #endif

@@ -81,6 +81,9 @@ struct MmaParams {
 
 __device__ uint32_t g_mma_status = 0u;
 __device__ unsigned long long g_mma_wait_limit = kWaitLimitCycles;
+// Test hook: warp 0 of CTA 0 expects its first unit's bytes but never copies A,
+// so its first stage wait runs out (failure detection without a GPU fault).
+__device__ int g_mma_test_drop = 0;
 
 __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
@@ -185,11 +188,13 @@ __global__ void __launch_bounds__(kWarps * 32) mma_gemm(const __grid_constant__ 
             if (lane == 0) {
                 const uint32_t bar = bars + 8u * s;
                 mbar_arrive_expect_tx(bar, static_cast<uint32_t>(x.nb * x.nt) * (kTileA + kTileB));
+                const bool drop = g_mma_test_drop != 0 && u == 0 && gw == 0;
                 for (int i = 0; i < x.nb; ++i) {
                     const long long bw = gw + (x.b0 + i) * nw;
                     const uint32_t j = static_cast<uint32_t>(i * x.nt);
-                    bulk_g2s(ring_s + s * kStageBytes + j * kTileA,
-                             p.a + bw * p.sa + static_cast<long long>(x.t0) * (kM * kK), x.nt * kTileA, bar);
+                    if (!drop)
+                        bulk_g2s(ring_s + s * kStageBytes + j * kTileA,
+                                 p.a + bw * p.sa + static_cast<long long>(x.t0) * (kM * kK), x.nt * kTileA, bar);
                     bulk_g2s(ring_s + s * kStageBytes + kStageA + j * kTileB,
                              p.b + bw * p.sb + static_cast<long long>(x.t0) * (kK * kN), x.nt * kTileB, bar);
                 }
@@ -411,6 +416,29 @@ int ncz_mma_matmul_batched(const void *a, const void *b, const void *c, void *d,
 
 int ncz_mma_matmul(const void *a, const void *b, const void *c, void *d, float alpha, float beta, void *stream) {
     return ncz_mma_matmul_batched(a, b, c, d, alpha, beta, 0, 0, 0, 1, stream);
+}
+
+namespace {
+int set_symbol_on(int device, const void *symbol, const void *value, size_t bytes) {
+    int prev = 0;
+    cudaError_t e = cudaGetDevice(&prev);
+    if (e != cudaSuccess) return ncz::map_cuda_error(e);
+    const int dev = device >= 0 ? device : prev;
+    if (dev != prev && (e = cudaSetDevice(dev)) != cudaSuccess) return ncz::map_cuda_error(e);
+    e = cudaMemcpyToSymbol(symbol, value, bytes);
+    if (dev != prev) cudaSetDevice(prev);
+    return e == cudaSuccess ? NCZ_SUCCESS : ncz::map_cuda_error(e);
+}
+}  // namespace
+
+int ncz_mma_test_set_wait_limit(int device, uint64_t cycles) {
+    const unsigned long long v = cycles != 0 ? cycles : nczm::kWaitLimitCycles;
+    return set_symbol_on(device, &nczm::g_mma_wait_limit, &v, sizeof(v));
+}
+
+int ncz_mma_test_drop_copy(int device, int enable) {
+    const int v = enable != 0;
+    return set_symbol_on(device, &nczm::g_mma_test_drop, &v, sizeof(v));
 }
 
 int ncz_mma_sync_status(int device) {

@@ -34,6 +34,8 @@ _SIGNATURES = {
     ),
     "ncz_mma_matmul": (ctypes.c_int, [_VP, _VP, _VP, _VP, ctypes.c_float, ctypes.c_float, _VP]),
     "ncz_mma_sync_status": (ctypes.c_int, [ctypes.c_int]),
+    "ncz_mma_test_set_wait_limit": (ctypes.c_int, [ctypes.c_int, ctypes.c_uint64]),
+    "ncz_mma_test_drop_copy": (ctypes.c_int, [ctypes.c_int, ctypes.c_int]),
 }
 _bound = False
 

@@ -140,3 +140,33 @@ def test_many_batches_grid_stride(ncz, oracle_mod):
     want = oracle_mod.mma_reference(a, b, c, alpha=1.0, beta=0.5, batch_stride_a=sa, batch_stride_b=sb,
                                     batch_stride_c=sc, k_iters=k_iters, epilogue=1, batches=batches)
     check(got, want, 1, "40000 batches")
+
+
+def test_stage_wait_times_out_cleanly(ncz):
+    """Failure detection without a GPU fault: with a short wait limit and one
+    bulk copy withheld, the stage wait runs out, the kernel stops cleanly and
+    the status reads DeviceTimeout; the next launch is correct."""
+    lib = ncz.mma.lib()
+    a, b, c, sa, sb, sc = problem(64, 4, 21)
+    try:
+        assert lib.ncz_mma_test_set_wait_limit(-1, 2_000_000) == 0  # about 1 ms
+        assert lib.ncz_mma_test_drop_copy(-1, 1) == 0
+        ta, tb, tc = dev(a), dev(b), dev(c)
+        td = torch.zeros_like(tc)
+        ncz.mma.pipelined_mma_matmul(ta, tb, tc, td, 1.0, 0.0, sa, sb, sc, 4, 0, 64)
+        with pytest.raises(ncz.FlashError) as err:
+            ncz.mma.sync_status()
+        assert "DeviceTimeout" in str(err.value)
+    finally:
+        lib.ncz_mma_test_drop_copy(-1, 0)
+        lib.ncz_mma_test_set_wait_limit(-1, 0)
+    got = run_pipelined(ncz, a, b, c, alpha=1.0, beta=0.0, sa=sa, sb=sb, sc=sc, k_iters=4, epilogue=0, batches=64)
+    want = ncz_oracle_mma(a, b, c, sa, sb, sc)
+    check(got, want, 0, "after timeout")
+
+
+def ncz_oracle_mma(a, b, c, sa, sb, sc):
+    from oracle import oracle as o
+
+    return o.mma_reference(a, b, c, alpha=1.0, beta=0.0, batch_stride_a=sa, batch_stride_b=sb, batch_stride_c=sc,
+                           k_iters=4, epilogue=0, batches=64)
