@@ -7,10 +7,12 @@
 // reach shared memory (TMA, or plain loads for misaligned strides).
 //
 // Work item: (batch x head slice, pair of 128-row Q tiles[, K range under
-// split-KV]); Q tile w covers rows q_base + 128 w .. + 127.  The grid has one
-// CTA per item (heaviest first), but a running CTA takes further items from
-// CTAs that have not started, through cluster launch control, so one CTA per
-// SM keeps pulling items in launch order.  Every role keeps running counters
+// split-KV]); Q tile w covers rows q_base + 128 w .. + 127.  Items are ordered
+// in chunks of slices whose K/V fits in L2, heaviest Q-tile group first inside
+// a chunk (make_work).  The grid has one CTA per item, but a running CTA takes
+// further items from CTAs that have not started, through cluster launch
+// control (asked for at the current item's last K/V tile), so one CTA per SM
+// keeps pulling items in launch order.  Every role keeps running counters
 // across items: the next item's Q (double-buffered), K/V (a kStages-deep ring
 // of 128-key tiles shared by both Q tiles) and first scores are fetched while
 // the current item's last tiles and epilogue run.
@@ -29,13 +31,13 @@
 //   warp 3       idle (keeps the softmax warpgroups warpgroup-aligned)
 //   warpgroup 1+w softmax for pipeline w (thread = row = TMEM lane)
 //
-// TMEM (512 columns): per Q tile w the scores S_w (128 cols f32, QK^T, M=128
-// N=128), the probabilities P_w (128 f16 keys = 64 cols, the A operand of PV
-// read from TMEM) and O_w (D <= 64 cols f32, PV, M=128 N=D).  The softmax
-// releases S_w as soon as the scores are in registers, so the MMA warp of Q
-// tile w issues QK_w(j+1) while the softmax is still exponentiating tile j;
-// PV_w(j) follows once P_w(j) is stored.  Each Q tile has its own MMA warp,
-// so neither tile's hand-offs wait behind the other's.
+// TMEM (512 columns): per pipeline w the scores S_w (128 cols f32, QK^T,
+// M=128 N=128), the probabilities P_w (128 f16 keys = 64 cols, the A operand
+// of PV read from TMEM) and O_w (D <= 64 cols f32, PV, M=128 N=D).  The
+// softmax releases S_w as soon as the scores are in registers, so MMA warp w
+// issues QK_w(j+1) while the softmax is still exponentiating tile j; PV_w(j)
+// follows once P_w(j) is stored.  Each pipeline has its own MMA warp, so
+// neither pipeline's hand-offs wait behind the other's.
 //
 // Online softmax (reference: src/flash_h64_bn32.zig:139-211) keeps the
 // exponent base m (log2 domain) and the row sum l in registers; O is
