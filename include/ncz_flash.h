@@ -180,6 +180,14 @@ int ncz_flash_sync_status(int device, void *stream, uint32_t *detail);
 
 /* --- Test hooks for the failure-detection path (device work, no fault). --- */
 
+/* Test hook: the work item `item` of a launch with this shape, split count
+ * (as ncz_flash_fwd_splits; 1 = none) and chunk of slices in the item order:
+ * out[0..7] = slice, first Q row, split, first K tile, K tiles of Q tile 0,
+ * of Q tile 1, their maximum, and the resolved split count.  Host only; no
+ * GPU needed.  NCZ_ERROR_INVALID_VALUE for an item outside the launch. */
+int ncz_test_item_work(size_t batch_heads, size_t seq_len, uint32_t causal, int splits, int chunk_slices, int item,
+                       int32_t *out);
+
 /* Bound of every in-kernel mbarrier wait on `device` (-1 = current), in SM
  * cycles; 0 restores the default (4e9, about 2 s).  A test shortens it so an
  * expired wait is seen quickly. */

@@ -729,6 +729,29 @@ int ncz_flash_sync_status(int device, void *stream, uint32_t *detail) {
     return word != 0 ? NCZ_ERROR_DEVICE_TIMEOUT : NCZ_SUCCESS;
 }
 
+int ncz_test_item_work(size_t batch_heads, size_t seq_len, uint32_t causal, int splits, int chunk_slices, int item,
+                       int32_t *out) {
+    if (out == nullptr || batch_heads == 0 || seq_len == 0 || splits < 1 || chunk_slices < 1 || item < 0 ||
+        seq_len > (size_t(1) << 30) || batch_heads > (size_t(1) << 20))
+        return NCZ_ERROR_INVALID_VALUE;
+    FlashParams p{};
+    p.batch_heads = static_cast<int>(batch_heads);
+    p.seq_len = static_cast<int>(seq_len);
+    p.causal = causal != 0;
+    p.num_groups = static_cast<int>((seq_len + kGroupRows - 1) / kGroupRows);
+    const int n_kv = static_cast<int>((seq_len + ncz::kBlockN - 1) / ncz::kBlockN);
+    const int want = std::min(splits, n_kv);
+    p.kv_per_split = (n_kv + want - 1) / want;  // as choose_splits
+    p.num_splits = (n_kv + p.kv_per_split - 1) / p.kv_per_split;
+    p.chunk_slices = static_cast<int>(std::min<size_t>(static_cast<size_t>(chunk_slices), batch_heads));
+    const long long items = static_cast<long long>(p.num_groups) * p.batch_heads * p.num_splits;
+    if (item >= items) return NCZ_ERROR_INVALID_VALUE;
+    const ncz::Work wk = ncz::make_work(p, item);
+    const int32_t vals[8] = {wk.slice, wk.q_base, wk.split, wk.kv0, wk.n[0], wk.n[1], wk.n_max, p.num_splits};
+    std::memcpy(out, vals, sizeof(vals));
+    return NCZ_SUCCESS;
+}
+
 int ncz_test_set_wait_limit(int device, uint64_t cycles) {
     int st = ncz_init();
     if (st != NCZ_SUCCESS) return st;

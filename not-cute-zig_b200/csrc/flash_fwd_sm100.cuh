@@ -203,7 +203,11 @@ __device__ unsigned long long g_ncz_wait_limit = kWaitLimitCycles;
 // signals its first scores, so the softmax's bounded wait runs out.
 __device__ int g_ncz_test_drop = 0;
 
-__device__ __forceinline__ Work make_work(const FlashParams &p, int item) {
+__host__ __device__ constexpr int imin(int a, int b) { return a < b ? a : b; }
+
+// Host and device: the host side checks the item order in tests
+// (ncz_test_item_work).
+__host__ __device__ __forceinline__ Work make_work(const FlashParams &p, int item) {
     Work wk;
     // Chunks of chunk_slices slices; inside a chunk the heaviest (last) Q-tile
     // groups first (under causal masking they visit the most K tiles), then
@@ -212,7 +216,7 @@ __device__ __forceinline__ Work make_work(const FlashParams &p, int item) {
     const int chunk = item / per_chunk;
     const int off = item - chunk * per_chunk;
     const int c0 = chunk * p.chunk_slices;
-    const int slices = min(p.chunk_slices, p.batch_heads - c0);  // the last chunk may be short
+    const int slices = imin(p.chunk_slices, p.batch_heads - c0);  // the last chunk may be short
     const int per_group = slices * p.num_splits;
     const int group = p.num_groups - 1 - off / per_group;
     const int rem = off % per_group;
@@ -225,10 +229,10 @@ __device__ __forceinline__ Work make_work(const FlashParams &p, int item) {
 #pragma unroll
     for (int w = 0; w < kQTiles; ++w) {
         const int q0 = wk.q_base + w * kBlockM;
-        const int last_row = min(q0 + kBlockM, p.seq_len) - 1;
+        const int last_row = imin(q0 + kBlockM, p.seq_len) - 1;
         // causal (reference tile_end, src/flash_h64_bn32.zig:80-84): K tiles up to the diagonal
         const int total = q0 >= p.seq_len ? 0 : (p.causal ? last_row / kBlockN + 1 : n_kv);
-        const int end = min(total, wk.kv0 + p.kv_per_split);
+        const int end = imin(total, wk.kv0 + p.kv_per_split);
         wk.n[w] = end > wk.kv0 ? end - wk.kv0 : 0;
         wk.diag[w] = total - 1;
         wk.n_max = wk.n[w] > wk.n_max ? wk.n[w] : wk.n_max;

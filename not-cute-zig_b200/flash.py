@@ -114,6 +114,8 @@ _SIGNATURES = {
     "ncz_flash_sync_status": (ctypes.c_int, [ctypes.c_int, _VP, ctypes.POINTER(ctypes.c_uint32)]),
     "ncz_test_set_wait_limit": (ctypes.c_int, [ctypes.c_int, ctypes.c_uint64]),
     "ncz_test_drop_arrive": (ctypes.c_int, [ctypes.c_int, ctypes.c_int]),
+    "ncz_test_item_work": (ctypes.c_int, [_SZ, _SZ, ctypes.c_uint32, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                          ctypes.POINTER(ctypes.c_int32)]),
     "ncz_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "ncz_launch_count": (ctypes.c_uint64, []),
     "ncz_umma_smem_desc": (ctypes.c_uint64, [ctypes.c_uint32] * 4),
