@@ -180,6 +180,16 @@ int ncz_flash_sync_status(int device, void *stream, uint32_t *detail);
 
 /* --- Test hooks for the failure-detection path (device work, no fault). --- */
 
+/* Test hook: the split-KV plan of a launch (host only, no GPU): requested 0 =
+ * automatic on `sms` SMs, 1 = none, n = up to n ranges; out[0] = ranges,
+ * out[1] = K tiles per range. */
+int ncz_test_split_plan(size_t batch_heads, size_t seq_len, int requested, size_t sms, int32_t *out);
+
+/* Test hook: the slice chunks of ncz_flash_fwd_host for a chunk size (taper =
+ * the tapered first and last chunks of the default plan); *count = chunks,
+ * out[0 .. count) their slice counts (NCZ_ERROR_OVERFLOW when cap is short). */
+int ncz_test_chunk_plan(size_t batch_heads, size_t chunk_slices, int taper, size_t *out, size_t cap, size_t *count);
+
 /* Test hook: the work item `item` of a launch with this shape, split count
  * (as ncz_flash_fwd_splits; 1 = none) and chunk of slices in the item order:
  * out[0..7] = slice, first Q row, split, first K tile, K tiles of Q tile 0,

@@ -284,12 +284,13 @@ int device_sms(int dev) {
 // half the SMs and the K range is long (>= 16 tiles; each range keeps >= 4).  A
 // CTA costs about the time of 4-5 K tiles in fixed set-up and hand-off, and the
 // merge is a second launch, so shorter ranges (config 2: 8 tiles) gain nothing.
-void choose_splits(const Resolved &r, int dev, int *splits, int *per_split) {
-    const int n_kv = static_cast<int>((r.seq + ncz::kBlockN - 1) / ncz::kBlockN);
-    const size_t ctas = ((r.seq + kGroupRows - 1) / kGroupRows) * r.bh;
-    int want = r.splits;
+// Split-KV ranges for a launch of bh slices of seq rows on `sms` SMs;
+// requested 0 = automatic, 1 = none, n = up to n ranges.
+void split_plan(size_t bh, size_t seq, int requested, size_t sms, int *splits, int *per_split) {
+    const int n_kv = static_cast<int>((seq + ncz::kBlockN - 1) / ncz::kBlockN);
+    const size_t ctas = ((seq + kGroupRows - 1) / kGroupRows) * bh;
+    int want = requested;
     if (want == 0) {
-        const size_t sms = static_cast<size_t>(device_sms(dev));
         want = 1;
         if (ctas * 2 <= sms && n_kv >= 16) {
             const int by_sms = static_cast<int>((sms + ctas - 1) / ctas);
@@ -300,6 +301,10 @@ void choose_splits(const Resolved &r, int dev, int *splits, int *per_split) {
     const int per = (n_kv + want - 1) / want;
     *per_split = per;
     *splits = (n_kv + per - 1) / per;
+}
+
+void choose_splits(const Resolved &r, int dev, int *splits, int *per_split) {
+    split_plan(r.bh, r.seq, r.splits, r.splits == 0 ? static_cast<size_t>(device_sms(dev)) : 0, splits, per_split);
 }
 
 // Validated launch on the current device (the caller switched devices).
@@ -727,6 +732,24 @@ int ncz_flash_sync_status(int device, void *stream, uint32_t *detail) {
     if (e != cudaSuccess) return map_cuda_error(e);
     if (detail != nullptr) *detail = word;
     return word != 0 ? NCZ_ERROR_DEVICE_TIMEOUT : NCZ_SUCCESS;
+}
+
+int ncz_test_split_plan(size_t batch_heads, size_t seq_len, int requested, size_t sms, int32_t *out) {
+    if (out == nullptr || batch_heads == 0 || seq_len == 0 || requested < 0 || sms == 0) return NCZ_ERROR_INVALID_VALUE;
+    int splits = 0, per = 0;
+    split_plan(batch_heads, seq_len, requested, sms, &splits, &per);
+    out[0] = splits;
+    out[1] = per;
+    return NCZ_SUCCESS;
+}
+
+int ncz_test_chunk_plan(size_t batch_heads, size_t chunk_slices, int taper, size_t *out, size_t cap, size_t *count) {
+    if (out == nullptr || count == nullptr || batch_heads == 0 || chunk_slices == 0) return NCZ_ERROR_INVALID_VALUE;
+    const std::vector<size_t> plan = chunk_plan(batch_heads, chunk_slices, taper != 0);
+    *count = plan.size();
+    if (plan.size() > cap) return NCZ_ERROR_OVERFLOW;
+    std::copy(plan.begin(), plan.end(), out);
+    return NCZ_SUCCESS;
 }
 
 int ncz_test_item_work(size_t batch_heads, size_t seq_len, uint32_t causal, int splits, int chunk_slices, int item,

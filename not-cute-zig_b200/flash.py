@@ -116,6 +116,9 @@ _SIGNATURES = {
     "ncz_test_drop_arrive": (ctypes.c_int, [ctypes.c_int, ctypes.c_int]),
     "ncz_test_item_work": (ctypes.c_int, [_SZ, _SZ, ctypes.c_uint32, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                           ctypes.POINTER(ctypes.c_int32)]),
+    "ncz_test_split_plan": (ctypes.c_int, [_SZ, _SZ, ctypes.c_int, _SZ, ctypes.POINTER(ctypes.c_int32)]),
+    "ncz_test_chunk_plan": (ctypes.c_int, [_SZ, _SZ, ctypes.c_int, ctypes.POINTER(ctypes.c_size_t), _SZ,
+                                           ctypes.POINTER(ctypes.c_size_t)]),
     "ncz_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "ncz_launch_count": (ctypes.c_uint64, []),
     "ncz_umma_smem_desc": (ctypes.c_uint64, [ctypes.c_uint32] * 4),
