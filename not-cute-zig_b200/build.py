@@ -1,5 +1,6 @@
 """Build recipe for libncz_flash.so (sm_100a only), in-tree: the flash-attention
-forward (csrc/flash_api.cu) and the batched GEMM with epilogue (csrc/mma_api.cu).
+forward (csrc/flash_api.cu), the batched GEMM with epilogue (csrc/mma_api.cu)
+and the driver-call table both of them call CUDA through (csrc/driver.cu).
 
 nvcc -gencode arch=compute_100a,code=sm_100a -O3 -lineinfo -shared -fPIC,
 static cudart (the library resolves cuTensorMapEncodeTiled at run time, so
@@ -21,7 +22,7 @@ FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17", "-li
 
 
 def sources():
-    return [os.path.join(HERE, "csrc", "flash_api.cu"), os.path.join(HERE, "csrc", "mma_api.cu")]
+    return [os.path.join(HERE, "csrc", f) for f in ("flash_api.cu", "mma_api.cu", "driver.cu")]
 
 
 def deps():

@@ -6,12 +6,11 @@
 //   selectKernel      src/flash.zig:72-96   -> ncz_flash_select
 //   CudaError/check   src/cuda.zig:134-178  -> ncz_status / map_cuda_error
 // The driver wrapper's single context (src/cuda.zig:181-196) becomes the
-// runtime's per-device primary contexts; cuTensorMapEncodeTiled is resolved
-// through cudaGetDriverEntryPointByVersion so the library has no link-time
-// dependency on libcuda (it loads on machines without a GPU driver).
+// runtime's per-device primary contexts.  Every CUDA call goes through the
+// driver-call table (driver.cu, include/ncz_driver.h), so host tests can fake
+// devices and fail chosen calls.
 #include <cuda.h>
 #include <cuda_runtime.h>
-#include <cudaTypedefs.h>
 
 #include <algorithm>
 #include <atomic>
@@ -21,6 +20,7 @@
 #include <mutex>
 #include <vector>
 
+#include "driver.cuh"
 #include "flash_fwd_sm100.cuh"
 #include "status.cuh"
 #include "ncz_flash.h"
@@ -47,10 +47,10 @@ constexpr int kVariants = 12;  // (D in 16/32/64) x (TMA, LSU) x (f16, bf16 inpu
 std::mutex g_mu;
 bool g_init_done = false;
 int g_init_status = NCZ_ERROR_NOT_INITIALIZED;
-PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::atomic<uint64_t> g_launches{0};
 bool g_attr_done[kMaxDevices][kVariants];
 
+using ncz::drv;
 using ncz::map_cuda_error;
 
 // Fully resolved launch description: row strides defaulted, dtype checked.
@@ -124,17 +124,11 @@ bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) %
 // 3-D map over one operand: dims (d, seq, bh), box (d, box_rows, 1), swizzle = row width.
 bool encode_map_uncached(CUtensorMap *map, const void *ptr, size_t d, size_t seq, size_t bh, size_t row,
                          size_t slice, uint32_t box_rows, bool bf16) {
-    cuuint64_t dims[3] = {d, seq, bh};
-    cuuint64_t strides[2] = {row * 2, slice * 2};
-    cuuint32_t box[3] = {static_cast<cuuint32_t>(d), box_rows, 1u};
-    cuuint32_t estr[3] = {1u, 1u, 1u};
-    const CUtensorMapSwizzle swz = d == 64 ? CU_TENSOR_MAP_SWIZZLE_128B
-                                           : (d == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
-    const CUresult res = g_encode(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
-                                  const_cast<void *>(ptr), dims, strides,
-                                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return res == CUDA_SUCCESS;
+    const uint64_t dims[3] = {d, seq, bh};
+    const uint64_t strides[2] = {row * 2, slice * 2};
+    const uint32_t box[3] = {static_cast<uint32_t>(d), box_rows, 1u};
+    const uint32_t swizzle = static_cast<uint32_t>(d * 2);  // one row: 32, 64 or 128 bytes
+    return drv().encode_tensor_map(map, bf16 ? 1 : 0, ptr, dims, strides, box, swizzle) == 0;
 }
 
 // Encoded maps, direct-mapped by their inputs.  A map is a pure function of
@@ -188,14 +182,15 @@ int launch_variant(const CUtensorMap &tq, const CUtensorMap &tk, const CUtensorM
         std::lock_guard<std::mutex> lock(g_mu);
         if (dev >= kMaxDevices) return NCZ_ERROR_INVALID_DEVICE;
         if (!g_attr_done[dev][vidx]) {
-            const cudaError_t e =
-                cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+            const int e = drv().set_max_dynamic_smem(reinterpret_cast<const void *>(kernel), L::kAlloc);
             if (e != cudaSuccess) return map_cuda_error(e);
             g_attr_done[dev][vidx] = true;
         }
     }
-    kernel<<<grid, ncz::kThreads, L::kAlloc, stream>>>(tq, tk, tv, p);
-    const cudaError_t e = cudaGetLastError();
+    void *args[4] = {const_cast<CUtensorMap *>(&tq), const_cast<CUtensorMap *>(&tk), const_cast<CUtensorMap *>(&tv),
+                     const_cast<FlashParams *>(&p)};
+    const int e = drv().launch_kernel(reinterpret_cast<const void *>(kernel), grid, ncz::kThreads, L::kAlloc, stream,
+                                      args);
     if (e != cudaSuccess) return map_cuda_error(e);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return NCZ_SUCCESS;
@@ -205,8 +200,9 @@ template <int D>
 int launch_combine(const FlashParams &p, cudaStream_t stream) {
     const long long rows = static_cast<long long>(p.batch_heads) * p.seq_len;
     const unsigned grid = static_cast<unsigned>((rows + 7) / 8);
-    ncz::combine_splits<D><<<grid, 256, 0, stream>>>(p);
-    const cudaError_t e = cudaGetLastError();
+    void *args[1] = {const_cast<FlashParams *>(&p)};
+    const int e = drv().launch_kernel(reinterpret_cast<const void *>(ncz::combine_splits<D>), grid, 256, 0, stream,
+                                      args);
     if (e != cudaSuccess) return map_cuda_error(e);
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return NCZ_SUCCESS;
@@ -222,7 +218,7 @@ int static_scratch(int dev, float **out) {
     std::lock_guard<std::mutex> lock(g_mu);
     if (g_scratch_addr[dev] == nullptr) {
         void *addr = nullptr;
-        const cudaError_t e = cudaGetSymbolAddress(&addr, g_ncz_scratch);
+        const int e = drv().symbol_address(&addr, static_cast<const void *>(&g_ncz_scratch));
         if (e != cudaSuccess) return map_cuda_error(e);
         g_scratch_addr[dev] = static_cast<float *>(addr);
     }
@@ -249,22 +245,16 @@ int launch_d(bool tma, bool bf16, const CUtensorMap &tq, const CUtensorMap &tk, 
 // Library-owned stream-ordered memory pool per device for split-KV partials:
 // allocations are ordered on the launch stream, so calls on different streams
 // never share a workspace, and the pool keeps freed memory for the next call.
-cudaMemPool_t g_pool[kMaxDevices];
+void *g_pool[kMaxDevices];
 int g_num_sms[kMaxDevices];
 
-int device_pool(int dev, cudaMemPool_t *pool) {
+int device_pool(int dev, void **pool) {
     std::lock_guard<std::mutex> lock(g_mu);
     if (g_pool[dev] == nullptr) {
-        cudaMemPoolProps props;
-        std::memset(&props, 0, sizeof(props));
-        props.allocType = cudaMemAllocationTypePinned;
-        props.location.type = cudaMemLocationTypeDevice;
-        props.location.id = dev;
-        cudaError_t e = cudaMemPoolCreate(&g_pool[dev], &props);
+        void *created = nullptr;
+        const int e = drv().pool_create(&created, dev, uint64_t(1) << 30);  // keep up to 1 GiB between calls
         if (e != cudaSuccess) return map_cuda_error(e);
-        uint64_t keep = uint64_t(1) << 30;  // keep up to 1 GiB between calls
-        e = cudaMemPoolSetAttribute(g_pool[dev], cudaMemPoolAttrReleaseThreshold, &keep);
-        if (e != cudaSuccess) return map_cuda_error(e);
+        g_pool[dev] = created;
     }
     *pool = g_pool[dev];
     return NCZ_SUCCESS;
@@ -274,7 +264,7 @@ int device_sms(int dev) {
     std::lock_guard<std::mutex> lock(g_mu);
     if (g_num_sms[dev] == 0) {
         int n = 0;
-        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+        if (drv().sm_count(dev, &n) != cudaSuccess || n <= 0) n = 148;
         g_num_sms[dev] = n;
     }
     return g_num_sms[dev];
@@ -371,10 +361,10 @@ int launch_on_current(const Resolved &r, int dev) {
         p.part_ml = p.part_o + rows * r.d;
     } else if (p.num_splits > 1) {
         const size_t rows = static_cast<size_t>(p.num_splits) * r.bh * r.seq;
-        cudaMemPool_t pool;
+        void *pool = nullptr;
         int st = device_pool(dev, &pool);
         if (st != NCZ_SUCCESS) return st;
-        const cudaError_t e = cudaMallocFromPoolAsync(&ws, rows * (r.d + 2) * sizeof(float), pool, r.stream);
+        const int e = drv().pool_alloc_async(&ws, rows * (r.d + 2) * sizeof(float), pool, r.stream);
         if (e != cudaSuccess) return map_cuda_error(e);
         p.part_o = static_cast<float *>(ws);
         p.part_ml = p.part_o + rows * r.d;
@@ -400,7 +390,7 @@ int launch_on_current(const Resolved &r, int dev) {
         default: st = launch_d<64>(use_tma, bf, tq, tk, tv, p, grid, dev, r.stream); break;
     }
     if (ws != nullptr) {
-        const cudaError_t e = cudaFreeAsync(ws, r.stream);
+        const int e = drv().free_async(ws, r.stream);
         if (st == NCZ_SUCCESS && e != cudaSuccess) st = map_cuda_error(e);
     }
     return st;
@@ -413,11 +403,12 @@ int launch_resolved(const Resolved &r) {
     st = ncz_init();
     if (st != NCZ_SUCCESS) return st;
     int prev = 0;
-    cudaError_t e = cudaGetDevice(&prev);
+    int e = drv().get_device(&prev);
     if (e != cudaSuccess) return map_cuda_error(e);
     const int dev = r.device >= 0 ? r.device : prev;
+    if (dev >= kMaxDevices) return NCZ_ERROR_INVALID_DEVICE;
     if (dev != prev) {
-        e = cudaSetDevice(dev);
+        e = drv().set_device(dev);
         if (e != cudaSuccess) return map_cuda_error(e);
     }
     if (r.use_static) {
@@ -428,7 +419,7 @@ int launch_resolved(const Resolved &r) {
     } else {
         st = launch_on_current(r, dev);
     }
-    if (dev != prev) cudaSetDevice(prev);
+    if (dev != prev) drv().set_device(prev);
     return st;
 }
 
@@ -453,18 +444,40 @@ Resolved reference_args(const void *q, const void *k, const void *v, void *o, si
 struct HostPipe {
     std::mutex mu;
     bool ready = false;
-    cudaStream_t up = nullptr, down = nullptr;
-    cudaEvent_t fork = nullptr, in_ready = nullptr, out_ready = nullptr, join = nullptr;
+    void *up = nullptr, *down = nullptr;                                       // streams
+    void *fork = nullptr, *in_ready = nullptr, *out_ready = nullptr, *join = nullptr;  // events
 };
 HostPipe g_pipes[kMaxDevices];
 
+// Destroys whatever of the pipe exists (hp.mu held); first error as a status.
+int pipe_release(HostPipe &hp) {
+    int first = cudaSuccess;
+    auto keep = [&first](int e) {
+        if (first == cudaSuccess) first = e;
+    };
+    for (void **ev : {&hp.fork, &hp.in_ready, &hp.out_ready, &hp.join}) {
+        if (*ev != nullptr) keep(drv().event_destroy(*ev));
+        *ev = nullptr;
+    }
+    for (void **st : {&hp.up, &hp.down}) {
+        if (*st != nullptr) keep(drv().stream_destroy(*st));
+        *st = nullptr;
+    }
+    hp.ready = false;
+    return map_cuda_error(first);
+}
+
+// Creates the pipe's streams and events; on a failure releases the ones made.
 int pipe_setup(HostPipe &hp) {
     if (hp.ready) return NCZ_SUCCESS;
-    cudaError_t e = cudaStreamCreateWithFlags(&hp.up, cudaStreamNonBlocking);
-    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&hp.down, cudaStreamNonBlocking);
-    cudaEvent_t *evs[4] = {&hp.fork, &hp.in_ready, &hp.out_ready, &hp.join};
-    for (int i = 0; i < 4 && e == cudaSuccess; ++i) e = cudaEventCreateWithFlags(evs[i], cudaEventDisableTiming);
-    if (e != cudaSuccess) return map_cuda_error(e);
+    int e = drv().stream_create(&hp.up);
+    if (e == cudaSuccess) e = drv().stream_create(&hp.down);
+    void **evs[4] = {&hp.fork, &hp.in_ready, &hp.out_ready, &hp.join};
+    for (int i = 0; i < 4 && e == cudaSuccess; ++i) e = drv().event_create(evs[i]);
+    if (e != cudaSuccess) {
+        pipe_release(hp);
+        return map_cuda_error(e);
+    }
     hp.ready = true;
     return NCZ_SUCCESS;
 }
@@ -504,9 +517,9 @@ int host_pipeline(const Resolved &r, const void *qh, const void *kh, const void 
     int st = pipe_setup(hp);
     if (st != NCZ_SUCCESS) return st;
     const size_t osz = r.o_dtype == NCZ_DTYPE_F32 ? 4 : 2;
-    cudaError_t e = cudaEventRecord(hp.fork, r.stream);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(hp.up, hp.fork, 0);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(hp.down, hp.fork, 0);
+    int e = drv().event_record(hp.fork, r.stream);
+    if (e == cudaSuccess) e = drv().stream_wait_event(hp.up, hp.fork);
+    if (e == cudaSuccess) e = drv().stream_wait_event(hp.down, hp.fork);
     if (e != cudaSuccess) return map_cuda_error(e);
     size_t s0 = 0;
     for (const size_t n_slices : chunk_plan(r.bh, chunk, taper)) {
@@ -518,13 +531,13 @@ int host_pipeline(const Resolved &r, const void *qh, const void *kh, const void 
         } in[3] = {{r.q, qh, r.qs, r.qr}, {r.k, kh, r.ks, r.kr}, {r.v, vh, r.vs, r.vr}};
         for (int i = 0; i < 3 && e == cudaSuccess; ++i) {
             const size_t off = s0 * in[i].slice * 2;
-            e = cudaMemcpyAsync(static_cast<char *>(const_cast<void *>(in[i].dev)) + off,
-                                static_cast<const char *>(in[i].host) + off,
-                                chunk_elems(s0, s1, in[i].slice, in[i].row, r.seq, r.d) * 2, cudaMemcpyHostToDevice,
-                                hp.up);
+            e = drv().memcpy_async(static_cast<char *>(const_cast<void *>(in[i].dev)) + off,
+                                   static_cast<const char *>(in[i].host) + off,
+                                   chunk_elems(s0, s1, in[i].slice, in[i].row, r.seq, r.d) * 2,
+                                   NCZ_COPY_HOST_TO_DEVICE, hp.up);
         }
-        if (e == cudaSuccess) e = cudaEventRecord(hp.in_ready, hp.up);
-        if (e == cudaSuccess) e = cudaStreamWaitEvent(r.stream, hp.in_ready, 0);
+        if (e == cudaSuccess) e = drv().event_record(hp.in_ready, hp.up);
+        if (e == cudaSuccess) e = drv().stream_wait_event(r.stream, hp.in_ready);
         if (e != cudaSuccess) return map_cuda_error(e);
         Resolved rc = r;
         rc.q = static_cast<const char *>(r.q) + s0 * r.qs * 2;
@@ -534,22 +547,103 @@ int host_pipeline(const Resolved &r, const void *qh, const void *kh, const void 
         rc.bh = s1 - s0;
         st = launch_on_current(rc, dev);
         if (st != NCZ_SUCCESS) return st;
-        e = cudaEventRecord(hp.out_ready, r.stream);
-        if (e == cudaSuccess) e = cudaStreamWaitEvent(hp.down, hp.out_ready, 0);
+        e = drv().event_record(hp.out_ready, r.stream);
+        if (e == cudaSuccess) e = drv().stream_wait_event(hp.down, hp.out_ready);
         if (e == cudaSuccess) {
             const size_t off = s0 * r.os * osz;
-            e = cudaMemcpyAsync(static_cast<char *>(oh) + off, static_cast<const char *>(r.o) + off,
-                                chunk_elems(s0, s1, r.os, r.orow, r.seq, r.d) * osz, cudaMemcpyDeviceToHost, hp.down);
+            e = drv().memcpy_async(static_cast<char *>(oh) + off, static_cast<const char *>(r.o) + off,
+                                   chunk_elems(s0, s1, r.os, r.orow, r.seq, r.d) * osz, NCZ_COPY_DEVICE_TO_HOST,
+                                   hp.down);
         }
         if (e != cudaSuccess) return map_cuda_error(e);
         s0 = s1;
     }
-    e = cudaEventRecord(hp.join, hp.down);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(r.stream, hp.join, 0);
+    e = drv().event_record(hp.join, hp.down);
+    if (e == cudaSuccess) e = drv().stream_wait_event(r.stream, hp.join);
     return e == cudaSuccess ? NCZ_SUCCESS : map_cuda_error(e);
 }
 
+// Switches to `device` (-1 = current), runs fn(), switches back.
+template <class Fn>
+int on_device(int device, Fn fn) {
+    int st = ncz_init();
+    if (st != NCZ_SUCCESS) return st;
+    int prev = 0;
+    int e = drv().get_device(&prev);
+    if (e != cudaSuccess) return map_cuda_error(e);
+    const int dev = device >= 0 ? device : prev;
+    if (dev != prev && (e = drv().set_device(dev)) != cudaSuccess) return map_cuda_error(e);
+    st = fn();
+    if (dev != prev) drv().set_device(prev);
+    return st;
+}
+
+int write_symbol(int device, const void *symbol, const void *value, size_t bytes) {
+    return on_device(device, [&] { return map_cuda_error(drv().symbol_write(symbol, value, bytes)); });
+}
+
 }  // namespace
+
+namespace ncz {
+
+int release_flash_objects() {
+    int first = NCZ_SUCCESS;
+    for (HostPipe &hp : g_pipes) {
+        std::lock_guard<std::mutex> lock(hp.mu);
+        const int st = pipe_release(hp);
+        if (first == NCZ_SUCCESS) first = st;
+    }
+    std::lock_guard<std::mutex> lock(g_mu);
+    for (void *&pool : g_pool) {
+        if (pool != nullptr) {
+            const int st = map_cuda_error(drv().pool_destroy(pool));
+            if (first == NCZ_SUCCESS) first = st;
+        }
+        pool = nullptr;
+    }
+    return first;
+}
+
+void reset_flash_caches() {
+    std::lock_guard<std::mutex> lock(g_mu);
+    std::memset(g_attr_done, 0, sizeof(g_attr_done));
+    for (MapSlot &m : g_maps) m.used = false;
+    std::memset(g_num_sms, 0, sizeof(g_num_sms));
+    std::memset(g_scratch_addr, 0, sizeof(g_scratch_addr));
+    g_init_done = false;
+    g_init_status = NCZ_ERROR_NOT_INITIALIZED;
+}
+
+template <int D, bool kTma, bool kBf16>
+const void *fwd_kernel() {
+    return reinterpret_cast<const void *>(flash_fwd_sm100<D, kTma, kBf16>);
+}
+
+template <int D>
+const void *combine_kernel() {
+    return reinterpret_cast<const void *>(combine_splits<D>);
+}
+
+const char *flash_kernel_label(const void *kernel) {
+    static const struct {
+        const void *fn;
+        const char *name;
+    } kNames[] = {
+        {fwd_kernel<16, true, false>(), "flash_fwd<16,tma,f16>"}, {fwd_kernel<16, true, true>(), "flash_fwd<16,tma,bf16>"},
+        {fwd_kernel<16, false, false>(), "flash_fwd<16,lsu,f16>"}, {fwd_kernel<16, false, true>(), "flash_fwd<16,lsu,bf16>"},
+        {fwd_kernel<32, true, false>(), "flash_fwd<32,tma,f16>"}, {fwd_kernel<32, true, true>(), "flash_fwd<32,tma,bf16>"},
+        {fwd_kernel<32, false, false>(), "flash_fwd<32,lsu,f16>"}, {fwd_kernel<32, false, true>(), "flash_fwd<32,lsu,bf16>"},
+        {fwd_kernel<64, true, false>(), "flash_fwd<64,tma,f16>"}, {fwd_kernel<64, true, true>(), "flash_fwd<64,tma,bf16>"},
+        {fwd_kernel<64, false, false>(), "flash_fwd<64,lsu,f16>"}, {fwd_kernel<64, false, true>(), "flash_fwd<64,lsu,bf16>"},
+        {combine_kernel<16>(), "combine_splits<16>"}, {combine_kernel<32>(), "combine_splits<32>"},
+        {combine_kernel<64>(), "combine_splits<64>"},
+    };
+    for (const auto &k : kNames)
+        if (k.fn == kernel) return k.name;
+    return nullptr;
+}
+
+}  // namespace ncz
 
 extern "C" {
 
@@ -557,7 +651,7 @@ int ncz_init(void) {
     std::lock_guard<std::mutex> lock(g_mu);
     if (g_init_done && g_init_status == NCZ_SUCCESS) return NCZ_SUCCESS;
     int count = 0;
-    cudaError_t e = cudaGetDeviceCount(&count);
+    const int e = drv().get_device_count(&count);
     if (e != cudaSuccess) {
         g_init_status = map_cuda_error(e);
         return g_init_status;
@@ -566,14 +660,10 @@ int ncz_init(void) {
         g_init_status = NCZ_ERROR_NO_DEVICE;
         return g_init_status;
     }
-    void *fn = nullptr;
-    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
-    e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q);
-    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr) {
+    if (drv().load_tensor_map_encoder() != cudaSuccess) {
         g_init_status = NCZ_ERROR_NOT_FOUND;
         return g_init_status;
     }
-    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
     g_init_done = true;
     g_init_status = NCZ_SUCCESS;
     return NCZ_SUCCESS;
@@ -585,7 +675,6 @@ int ncz_shutdown(void) {
     for (MapSlot &m : g_maps) m.used = false;
     g_init_done = false;
     g_init_status = NCZ_ERROR_NOT_INITIALIZED;
-    g_encode = nullptr;
     return NCZ_SUCCESS;
 }
 
@@ -690,12 +779,12 @@ int ncz_flash_fwd_host(const ncz_flash_desc *desc, const void *q_host, const voi
     st = ncz_init();
     if (st != NCZ_SUCCESS) return st;
     int prev = 0;
-    cudaError_t e = cudaGetDevice(&prev);
+    int e = drv().get_device(&prev);
     if (e != cudaSuccess) return map_cuda_error(e);
     const int dev = r.device >= 0 ? r.device : prev;
     if (dev >= kMaxDevices) return NCZ_ERROR_INVALID_DEVICE;
     if (dev != prev) {
-        e = cudaSetDevice(dev);
+        e = drv().set_device(dev);
         if (e != cudaSuccess) return map_cuda_error(e);
     }
     // Default: 8 chunks, so one chunk's upload hides the previous chunk's forward,
@@ -708,28 +797,24 @@ int ncz_flash_fwd_host(const ncz_flash_desc *desc, const void *q_host, const voi
         chunk = std::max((r.bh + 7) / 8, min_slices);
     }
     st = host_pipeline(r, q_host, k_host, v_host, o_host, chunk, chunk_slices == 0, dev);
-    if (dev != prev) cudaSetDevice(prev);
+    if (dev != prev) drv().set_device(prev);
     return st;
 }
 
 int ncz_flash_sync_status(int device, void *stream, uint32_t *detail) {
     if (detail != nullptr) *detail = 0;
-    int st = ncz_init();
-    if (st != NCZ_SUCCESS) return st;
-    int prev = 0;
-    cudaError_t e = cudaGetDevice(&prev);
-    if (e != cudaSuccess) return map_cuda_error(e);
-    const int dev = device >= 0 ? device : prev;
-    if (dev != prev && (e = cudaSetDevice(dev)) != cudaSuccess) return map_cuda_error(e);
     uint32_t word = 0;
-    e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
-    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&word, ncz::g_ncz_status, sizeof(word));
-    if (e == cudaSuccess && word != 0) {
-        const uint32_t zero = 0;
-        e = cudaMemcpyToSymbol(ncz::g_ncz_status, &zero, sizeof(zero));
-    }
-    if (dev != prev) cudaSetDevice(prev);
-    if (e != cudaSuccess) return map_cuda_error(e);
+    const int st = on_device(device, [&] {
+        const void *sym = static_cast<const void *>(&ncz::g_ncz_status);
+        int e = drv().stream_synchronize(stream);
+        if (e == cudaSuccess) e = drv().symbol_read(&word, sym, sizeof(word));
+        if (e == cudaSuccess && word != 0) {
+            const uint32_t zero = 0;
+            e = drv().symbol_write(sym, &zero, sizeof(zero));
+        }
+        return map_cuda_error(e);
+    });
+    if (st != NCZ_SUCCESS) return st;
     if (detail != nullptr) *detail = word;
     return word != 0 ? NCZ_ERROR_DEVICE_TIMEOUT : NCZ_SUCCESS;
 }
@@ -776,31 +861,13 @@ int ncz_test_item_work(size_t batch_heads, size_t seq_len, uint32_t causal, int 
 }
 
 int ncz_test_set_wait_limit(int device, uint64_t cycles) {
-    int st = ncz_init();
-    if (st != NCZ_SUCCESS) return st;
-    int prev = 0;
-    cudaError_t e = cudaGetDevice(&prev);
-    if (e != cudaSuccess) return map_cuda_error(e);
-    const int dev = device >= 0 ? device : prev;
-    if (dev != prev && (e = cudaSetDevice(dev)) != cudaSuccess) return map_cuda_error(e);
     const unsigned long long v = cycles != 0 ? cycles : ncz::kWaitLimitCycles;
-    e = cudaMemcpyToSymbol(ncz::g_ncz_wait_limit, &v, sizeof(v));
-    if (dev != prev) cudaSetDevice(prev);
-    return e == cudaSuccess ? NCZ_SUCCESS : map_cuda_error(e);
+    return write_symbol(device, static_cast<const void *>(&ncz::g_ncz_wait_limit), &v, sizeof(v));
 }
 
 int ncz_test_drop_arrive(int device, int enable) {
-    int st = ncz_init();
-    if (st != NCZ_SUCCESS) return st;
-    int prev = 0;
-    cudaError_t e = cudaGetDevice(&prev);
-    if (e != cudaSuccess) return map_cuda_error(e);
-    const int dev = device >= 0 ? device : prev;
-    if (dev != prev && (e = cudaSetDevice(dev)) != cudaSuccess) return map_cuda_error(e);
     const int v = enable != 0;
-    e = cudaMemcpyToSymbol(ncz::g_ncz_test_drop, &v, sizeof(v));
-    if (dev != prev) cudaSetDevice(prev);
-    return e == cudaSuccess ? NCZ_SUCCESS : map_cuda_error(e);
+    return write_symbol(device, static_cast<const void *>(&ncz::g_ncz_test_drop), &v, sizeof(v));
 }
 
 const char *ncz_status_string(int status) {

@@ -35,8 +35,10 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <cstring>
 #include <mutex>
 
+#include "driver.cuh"
 #include "ncz_flash.h"
 #include "ncz_mma.h"
 #include "sm100_ptx.cuh"
@@ -332,24 +334,29 @@ bool g_attr_done[kMaxDevices][2];
 int g_sms[kMaxDevices];
 
 template <bool kBcol>
-int launch(const nczm::MmaParams &p, cudaStream_t stream) {
+const void *gemm_kernel() {
+    return reinterpret_cast<const void *>(nczm::mma_gemm<kBcol>);
+}
+
+template <bool kBcol>
+int launch(const nczm::MmaParams &p, void *stream) {
     if (p.batches == 0) return NCZ_SUCCESS;
+    const ncz_driver_table &drv = ncz::drv();
     int dev = 0;
-    cudaError_t e = cudaGetDevice(&dev);
+    int e = drv.get_device(&dev);
     if (e != cudaSuccess) return ncz::map_cuda_error(e);
     if (dev < 0 || dev >= kMaxDevices) return NCZ_ERROR_INVALID_DEVICE;
     int sms;
     {
         std::lock_guard<std::mutex> lock(g_mu);
         if (!g_attr_done[dev][kBcol]) {
-            e = cudaFuncSetAttribute(nczm::mma_gemm<kBcol>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(nczm::kSmemBytes));
+            e = drv.set_max_dynamic_smem(gemm_kernel<kBcol>(), static_cast<int>(nczm::kSmemBytes));
             if (e != cudaSuccess) return ncz::map_cuda_error(e);
             g_attr_done[dev][kBcol] = true;
         }
         if (g_sms[dev] == 0) {
             int n = 0;
-            if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+            if (drv.sm_count(dev, &n) != cudaSuccess || n <= 0) n = 148;
             g_sms[dev] = n;
         }
         sms = g_sms[dev];
@@ -357,8 +364,9 @@ int launch(const nczm::MmaParams &p, cudaStream_t stream) {
     // Two CTAs (16 warps, 2 x 98 KB of stages) per SM; warps stride over batches.
     const long long need = (p.batches + nczm::kWarps - 1) / nczm::kWarps;
     const unsigned grid = static_cast<unsigned>(std::min<long long>(need, 2LL * sms));
-    nczm::mma_gemm<kBcol><<<grid, nczm::kWarps * 32, nczm::kSmemBytes, stream>>>(p);
-    return ncz::map_cuda_error(cudaGetLastError());
+    void *args[1] = {const_cast<nczm::MmaParams *>(&p)};
+    return ncz::map_cuda_error(
+        drv.launch_kernel(gemm_kernel<kBcol>(), grid, nczm::kWarps * 32, nczm::kSmemBytes, stream, args));
 }
 
 bool aligned16(const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
@@ -401,7 +409,7 @@ int ncz_mma_matmul_pipelined(const void *a, const void *b, const void *c, void *
     int st = fill_params(p, a, b, c, d, alpha, beta, batch_stride_a, batch_stride_b, batch_stride_c, k_iters,
                          epilogue, batches);
     if (st != NCZ_SUCCESS) return st;
-    return launch<false>(p, static_cast<cudaStream_t>(stream));
+    return launch<false>(p, stream);
 }
 
 int ncz_mma_matmul_batched(const void *a, const void *b, const void *c, void *d, float alpha, float beta,
@@ -411,25 +419,36 @@ int ncz_mma_matmul_batched(const void *a, const void *b, const void *c, void *d,
     int st = fill_params(p, a, b, c, d, alpha, beta, batch_stride_a, batch_stride_b, batch_stride_c, 1,
                          NCZ_EPILOGUE_NONE, batches);
     if (st != NCZ_SUCCESS) return st;
-    return launch<true>(p, static_cast<cudaStream_t>(stream));
+    return launch<true>(p, stream);
 }
 
 int ncz_mma_matmul(const void *a, const void *b, const void *c, void *d, float alpha, float beta, void *stream) {
     return ncz_mma_matmul_batched(a, b, c, d, alpha, beta, 0, 0, 0, 1, stream);
 }
 
+}  // extern "C"
+
 namespace {
-int set_symbol_on(int device, const void *symbol, const void *value, size_t bytes) {
+// Switches to `device` (-1 = current), runs fn() (a CUDA error number), switches back.
+template <class Fn>
+int on_device(int device, Fn fn) {
+    const ncz_driver_table &drv = ncz::drv();
     int prev = 0;
-    cudaError_t e = cudaGetDevice(&prev);
+    int e = drv.get_device(&prev);
     if (e != cudaSuccess) return ncz::map_cuda_error(e);
     const int dev = device >= 0 ? device : prev;
-    if (dev != prev && (e = cudaSetDevice(dev)) != cudaSuccess) return ncz::map_cuda_error(e);
-    e = cudaMemcpyToSymbol(symbol, value, bytes);
-    if (dev != prev) cudaSetDevice(prev);
-    return e == cudaSuccess ? NCZ_SUCCESS : ncz::map_cuda_error(e);
+    if (dev != prev && (e = drv.set_device(dev)) != cudaSuccess) return ncz::map_cuda_error(e);
+    e = fn();
+    if (dev != prev) drv.set_device(prev);
+    return ncz::map_cuda_error(e);
+}
+
+int set_symbol_on(int device, const void *symbol, const void *value, size_t bytes) {
+    return on_device(device, [&] { return ncz::drv().symbol_write(symbol, value, bytes); });
 }
 }  // namespace
+
+extern "C" {
 
 int ncz_mma_test_set_wait_limit(int device, uint64_t cycles) {
     const unsigned long long v = cycles != 0 ? cycles : nczm::kWaitLimitCycles;
@@ -442,21 +461,36 @@ int ncz_mma_test_drop_copy(int device, int enable) {
 }
 
 int ncz_mma_sync_status(int device) {
-    int prev = 0;
-    cudaError_t e = cudaGetDevice(&prev);
-    if (e != cudaSuccess) return ncz::map_cuda_error(e);
-    const int dev = device >= 0 ? device : prev;
-    if (dev != prev && (e = cudaSetDevice(dev)) != cudaSuccess) return ncz::map_cuda_error(e);
     uint32_t word = 0;
-    e = cudaDeviceSynchronize();
-    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&word, nczm::g_mma_status, sizeof(word));
-    if (e == cudaSuccess && word != 0) {
-        const uint32_t zero = 0;
-        e = cudaMemcpyToSymbol(nczm::g_mma_status, &zero, sizeof(zero));
-    }
-    if (dev != prev) cudaSetDevice(prev);
-    if (e != cudaSuccess) return ncz::map_cuda_error(e);
+    const int st = on_device(device, [&] {
+        const ncz_driver_table &drv = ncz::drv();
+        const void *sym = static_cast<const void *>(&nczm::g_mma_status);
+        int e = drv.device_synchronize();
+        if (e == cudaSuccess) e = drv.symbol_read(&word, sym, sizeof(word));
+        if (e == cudaSuccess && word != 0) {
+            const uint32_t zero = 0;
+            e = drv.symbol_write(sym, &zero, sizeof(zero));
+        }
+        return e;
+    });
+    if (st != NCZ_SUCCESS) return st;
     return word != 0 ? NCZ_ERROR_DEVICE_TIMEOUT : NCZ_SUCCESS;
 }
 
 }  // extern "C"
+
+namespace ncz {
+
+void reset_mma_caches() {
+    std::lock_guard<std::mutex> lock(g_mu);
+    std::memset(g_attr_done, 0, sizeof(g_attr_done));
+    std::memset(g_sms, 0, sizeof(g_sms));
+}
+
+const char *mma_kernel_label(const void *kernel) {
+    if (kernel == gemm_kernel<false>()) return "mma_gemm<row_b>";
+    if (kernel == gemm_kernel<true>()) return "mma_gemm<col_b>";
+    return nullptr;
+}
+
+}  // namespace ncz

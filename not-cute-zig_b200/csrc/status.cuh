@@ -31,4 +31,7 @@ inline int map_cuda_error(cudaError_t e) {
     }
 }
 
+// Driver-call table entries return the runtime's error numbers as int.
+inline int map_cuda_error(int e) { return map_cuda_error(static_cast<cudaError_t>(e)); }
+
 }  // namespace ncz
