@@ -12,6 +12,7 @@ src/main.zig:1042); rel = |a - b| / max(|b|, 1e-3).
 
     python not-cute-zig_b200/compare.py                  # the 15 reference shapes
     python not-cute-zig_b200/compare.py --shape 8,1024,64,1 --gpus 2 --jsonl out.jsonl
+    python not-cute-zig_b200/compare.py --shape 4,1000,32,1 --row-stride 40 --in-dtype bf16 --o-dtype f16 --seed 7
     python not-cute-zig_b200/compare.py --mma        # GEMM + epilogue (compareMma, src/main.zig:953-975)
 """
 from __future__ import annotations
@@ -45,12 +46,14 @@ def fill_flash_input(n: int, mul: int, add: int, scale: float):
     return (((i * mul + add) % 17).astype(np.float32) * np.float32(scale)).astype(np.float16)
 
 
-def torch_attention(q, k, v, bh: int, s: int, d: int, scale: float, causal: bool):
+def torch_attention(q, k, v, bh: int, s: int, d: int, scale: float, causal: bool, row: int = 0):
     """fp32 attention in torch (cross-check only): softmax(QK^T * scale, causal
-    top-left) V, per slice."""
+    top-left) V, per slice; rows `row` elements apart (0 = d), flat result of
+    bh * s * d elements."""
     import torch
 
-    qf, kf, vf = (t.view(bh, s, d).float() for t in (q, k, v))
+    row = row or d
+    qf, kf, vf = (t.view(bh, s, row)[:, :, :d].float() for t in (q, k, v))
     scores = torch.matmul(qf, kf.transpose(1, 2)) * scale
     if causal:
         mask = torch.ones(s, s, dtype=torch.bool, device=q.device).triu(1)
@@ -67,32 +70,57 @@ def measured_peak() -> Optional[float]:
         return None
 
 
-def compare_shape(ncz, bh: int, s: int, d: int, causal: bool, gpus: int = 1) -> dict:
+IN_DTYPES = {"f16": "float16", "bf16": "bfloat16"}
+O_DTYPES = {"f32": ("float32", 4), "f16": ("float16", 2), "bf16": ("bfloat16", 2)}
+
+
+def compare_shape(ncz, bh: int, s: int, d: int, causal: bool, gpus: int = 1, *, seed: Optional[int] = None,
+                  in_dtype: str = "f16", o_dtype: str = "f32", row_stride: int = 0) -> dict:
+    """One compareFlash record.  Defaults are the reference's: fillFlashInput
+    inputs, f16 Q/K/V, f32 O, rows of head_dim elements, through flash.launch.
+    `seed` draws N(0, 1) inputs instead; `in_dtype` / `o_dtype` / `row_stride`
+    (elements between rows, >= head_dim; the padding of O must stay untouched)
+    go through the extended descriptor (flash.launch_ex)."""
+    import numpy as np
     import torch
 
     from importlib import import_module
 
     bench = import_module("not-cute-zig_b200.benchmark")
     shard = import_module("not-cute-zig_b200.shard")
-    stride = s * d
+    row = row_stride or d
+    if row < d:
+        raise ValueError(f"row stride {row} < head_dim {d}")
+    extended = row != d or in_dtype != "f16" or o_dtype != "f32"
+    in_torch = getattr(torch, IN_DTYPES[in_dtype])
+    o_name, o_bytes = O_DTYPES[o_dtype]
+    o_torch = getattr(torch, o_name)
+    stride = s * row
     n = bh * stride
     scale = 1.0 / math.sqrt(d)
-    hq, hk, hv = fill_flash_input(n, 3, 1, 0.125), fill_flash_input(n, 5, 2, 0.0625), fill_flash_input(n, 7, 3, 0.03125)
+    if seed is None:
+        hq, hk, hv = (fill_flash_input(n, 3, 1, 0.125), fill_flash_input(n, 5, 2, 0.0625),
+                      fill_flash_input(n, 7, 3, 0.03125))
+    else:
+        rng = np.random.default_rng(seed)
+        hq, hk, hv = (rng.standard_normal(n, dtype=np.float32) for _ in range(3))
     flops = bh * (4 * ((s * (s + 1)) // 2 if causal else s * s) * d)
-    bytes_ = n * (2 * 3 + 4)
+    bytes_ = bh * s * d * (2 * 3 + o_bytes)
     gpus = max(1, min(gpus, torch.cuda.device_count(), bh))
     launches, streams, outs = [], [], []
     for g in range(gpus):
         lo, hi = shard.slice_range(bh, gpus, g)
         dev = torch.device("cuda", g)
-        q = torch.from_numpy(hq[lo * stride:hi * stride]).to(dev)
-        k = torch.from_numpy(hk[lo * stride:hi * stride]).to(dev)
-        v = torch.from_numpy(hv[lo * stride:hi * stride]).to(dev)
-        o = torch.zeros((hi - lo) * stride, dtype=torch.float32, device=dev)
+        q, k, v = (torch.from_numpy(h[lo * stride:hi * stride]).to(dev).to(in_torch) for h in (hq, hk, hv))
+        o = torch.zeros((hi - lo) * stride, dtype=o_torch, device=dev)
         st = torch.cuda.Stream(dev)
         opts = ncz.Options(seq_len=s, head_dim=d, q_stride=stride, k_stride=stride, v_stride=stride,
                            o_stride=stride, scale=scale, batch_heads=hi - lo, causal=causal)
-        launches.append(lambda q=q, k=k, v=v, o=o, opts=opts, st=st: ncz.launch(q, k, v, o, opts, stream=st))
+        if extended:
+            launches.append(lambda q=q, k=k, v=v, o=o, opts=opts, st=st: ncz.launch_ex(
+                q, k, v, o, opts, row_strides=(row,) * 4, stream=st))
+        else:
+            launches.append(lambda q=q, k=k, v=v, o=o, opts=opts, st=st: ncz.launch(q, k, v, o, opts, stream=st))
         streams.append(st)
         outs.append((q, k, v, o, lo, hi))
     if gpus == 1:
@@ -102,20 +130,27 @@ def compare_shape(ncz, bh: int, s: int, d: int, causal: bool, gpus: int = 1) -> 
     else:
         res = bench.run_multi(launches, streams, warmup_iters=5, iters=20, bytes_processed=bytes_,
                               flops_processed=flops)
-    max_abs, max_rel = 0.0, 0.0
+    max_abs, max_rel, padding_kept = 0.0, 0.0, True
     for (q, k, v, o, lo, hi), st in zip(outs, streams):
         st.synchronize()
         ncz.sync_status(device=q.device.index, stream=st)
-        want = torch_attention(q, k, v, hi - lo, s, d, scale, causal)
-        diff = (o - want).abs()
+        want = torch_attention(q, k, v, hi - lo, s, d, scale, causal, row)
+        got = o.view(hi - lo, s, row)
+        diff = (got[:, :, :d].float().reshape(-1) - want).abs()
         max_abs = max(max_abs, float(diff.max()))
         max_rel = max(max_rel, float((diff / want.abs().clamp_min(1e-3)).max()))
+        padding_kept = padding_kept and bool((got[:, :, d:] == 0).all())
     peak = measured_peak()
     shape = f"batch_heads={bh},seq={s},head={d},causal={str(causal).lower()}"
+    if extended:
+        shape += f",row_stride={row},in={in_dtype},o={o_dtype}"
+    if seed is not None:
+        shape += f",seed={seed}"
     label = ncz.select_kernel(ncz.Options(seq_len=s, head_dim=d, q_stride=stride, k_stride=stride,
                                           v_stride=stride, o_stride=stride, scale=scale, batch_heads=bh,
                                           causal=causal)).label
-    return res.record("flash_attention", "not_cute_zig_b200", shape, max_abs <= 0.02, bytes_, flops, max_abs,
+    return res.record("flash_attention", "not_cute_zig_b200", shape, max_abs <= 0.02 and padding_kept, bytes_,
+                      flops, max_abs,
                       gpus=gpus, device_ms=res.device_ms, host_ms=res.host_ms,
                       pct_peak_nominal=(res.tflops or 0.0) / NOMINAL_F16_TFLOPS,
                       pct_peak_measured=((res.tflops or 0.0) / peak) if peak else None,
@@ -201,6 +236,12 @@ def main(argv=None) -> int:
     ap.add_argument("--shape", action="append", default=[],
                     help="bh,seq,head,causal (repeatable); default: the 15 reference compare shapes")
     ap.add_argument("--gpus", type=int, default=1, help="shard slices across this many devices")
+    ap.add_argument("--seed", type=int, default=None,
+                    help="N(0,1) inputs from this seed instead of the reference's fillFlashInput pattern")
+    ap.add_argument("--in-dtype", choices=sorted(IN_DTYPES), default="f16", help="Q/K/V element type")
+    ap.add_argument("--o-dtype", choices=sorted(O_DTYPES), default="f32", help="O element type")
+    ap.add_argument("--row-stride", type=int, default=0,
+                    help="elements between rows of Q/K/V/O (>= head_dim; 0 = head_dim)")
     ap.add_argument("--jsonl", default=None, help="append records to this file instead of stdout")
     ap.add_argument("--mma", action="store_true",
                     help="the GEMM + epilogue records instead: compareMma's 16x8x16 and batched throughput shapes")
@@ -220,7 +261,8 @@ def main(argv=None) -> int:
         for spec in args.shape:
             bh, s, d, c = (int(x) for x in spec.split(","))
             shapes.append((bh, s, d, bool(c)))
-    records = [compare_shape(ncz, bh, s, d, c, args.gpus) for bh, s, d, c in shapes]
+    records = [compare_shape(ncz, bh, s, d, c, args.gpus, seed=args.seed, in_dtype=args.in_dtype,
+                             o_dtype=args.o_dtype, row_stride=args.row_stride) for bh, s, d, c in shapes]
     bench.emit(records, args.jsonl)
     return 0 if all(r["correct"] for r in records) else 1
 

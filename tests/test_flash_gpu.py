@@ -426,6 +426,25 @@ def test_compare_harness_records(ncz):
         assert rec["label"] == f"flash_fwd_sm100a_d{d}"
 
 
+def test_compare_cli_layout_and_type_flags(ncz, tmp_path):
+    """compare.py's --seed / --in-dtype / --o-dtype / --row-stride: N(0,1)
+    inputs, padded rows (O padding untouched), bf16 inputs, f16 and bf16 O,
+    each within the compare bound against fp32 torch attention."""
+    import importlib
+    import json
+
+    compare = importlib.import_module("not-cute-zig_b200.compare")
+    out = tmp_path / "records.jsonl"
+    argv = ["--shape", "4,1000,32,1", "--shape", "2,300,64,0", "--row-stride", "72", "--seed", "7",
+            "--jsonl", str(out)]
+    for in_dtype, o_dtype in (("f16", "f32"), ("bf16", "f16"), ("f16", "bf16")):
+        assert compare.main(argv + ["--in-dtype", in_dtype, "--o-dtype", o_dtype]) == 0
+    recs = [json.loads(line) for line in out.read_text().splitlines()]
+    assert len(recs) == 6 and all(r["correct"] for r in recs)
+    assert all("row_stride=72" in r["shape"] and "seed=7" in r["shape"] for r in recs)
+    assert max(r["max_abs_error"] for r in recs[:2]) <= 2e-3  # f32 O: the parity bound
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_compare_harness_multi_device(ncz):
     import importlib
