@@ -103,10 +103,11 @@ int ncz_flash_validate(size_t batch_heads, size_t seq_len, size_t head_dim, size
  * head_dim), o_dtype and producer in range. */
 int ncz_flash_validate_ex(const ncz_flash_desc *desc);
 
-/* flash.selectKernel (src/flash.zig:72-96).  Writes the kernel label (e.g.
- * "flash_fwd_sm100a_d64_tma") into `label` (NUL-terminated, truncated to
- * `cap`) and the threads per CTA into *threads.  One sm_100a kernel family
- * replaces flash_attention_fwd_{opt,v2,h64,h64_bn32,h64_causal}. */
+/* flash.selectKernel (src/flash.zig:72-96).  Writes the kernel label
+ * ("flash_fwd_sm100a_d16", "_d32" or "_d64") into `label` (NUL-terminated,
+ * truncated to `cap`) and the threads per CTA into *threads.  One sm_100a
+ * kernel family replaces flash_attention_fwd_{opt,v2,h64,h64_bn32,h64_causal};
+ * ncz_flash_fwd_named accepts those names and these labels. */
 int ncz_flash_select(size_t batch_heads, size_t seq_len, size_t head_dim, uint32_t causal,
                      char *label, size_t cap, uint32_t *threads);
 
@@ -117,6 +118,34 @@ int ncz_flash_select(size_t batch_heads, size_t seq_len, size_t head_dim, uint32
 int ncz_flash_fwd(const void *q, const void *k, const void *v, void *o, size_t batch_heads,
                   size_t seq_len, size_t head_dim, size_t q_stride, size_t k_stride,
                   size_t v_stride, size_t o_stride, float scale, uint32_t causal, void *stream);
+
+/* module.getFunction(name) + Function.launch(cfg, tuple) of the reference's
+ * callers (src/main.zig:93-94, :820-852): launches the kernel named `kernel`
+ * with the 12-argument tuple and batch_heads (grid.y).  Accepted names are the
+ * reference's exported flash kernels and this library's labels:
+ *   flash_attention_fwd          d 16/32/64          src/kernels.zig:380-394
+ *   flash_attention_fwd_opt      d 16/32/64          src/flash_opt.zig:17-31
+ *   flash_attention_fwd_v2       d 16/32/64          src/flash_v2.zig:23-37
+ *   flash_attention_fwd_h64      d 64                src/flash_h64.zig:21-35
+ *   flash_attention_fwd_h64_bn32 d 64                src/flash_h64_bn32.zig:26-40
+ *   flash_attention_fwd_h64_causal d 64, always causal (ignores `causal`)
+ *                                                    src/flash_h64_causal.zig:20-35
+ *   flash_fwd_sm100a_d16 / _d32 / _d64  that head_dim only
+ * As each of those kernels does, a call with seq_len 0 or a head_dim the name
+ * does not accept returns NCZ_SUCCESS without launching or writing O.  Any
+ * other name is NCZ_ERROR_NOT_FOUND (cuModuleGetFunction's answer);
+ * batch_heads 0 is NCZ_ERROR_INVALID_VALUE (a launch with grid.y 0).  The
+ * reference kernels check no strides; here they are validated as in
+ * ncz_flash_fwd. */
+int ncz_flash_fwd_named(const char *kernel, const void *q, const void *k, const void *v, void *o,
+                        size_t batch_heads, size_t seq_len, size_t head_dim, size_t q_stride,
+                        size_t k_stride, size_t v_stride, size_t o_stride, float scale, uint32_t causal,
+                        void *stream);
+
+/* Head dimensions (bit 0: 16, bit 1: 32, bit 2: 64) and forced causality
+ * (1 = always causal) of a kernel name accepted by ncz_flash_fwd_named;
+ * NCZ_ERROR_NOT_FOUND for any other name. */
+int ncz_flash_kernel_info(const char *kernel, uint32_t *head_dims, uint32_t *always_causal);
 
 /* flash.launch (src/flash.zig:31-70): like ncz_flash_fwd, but takes the
  * slice lengths (elements) so requireLen (src/flash.zig:98-100) is checked:

@@ -16,6 +16,7 @@ from .flash import (  # noqa: F401
     launch_ex,
     launch_host,
     launch_multi,
+    launch_named,
     launch_splits,
     launch_static,
     select_kernel,

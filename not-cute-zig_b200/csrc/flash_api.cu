@@ -437,6 +437,33 @@ Resolved reference_args(const void *q, const void *k, const void *v, void *o, si
     return from_desc(desc);
 }
 
+// Kernel names ncz_flash_fwd_named accepts: the reference's exported flash
+// kernels (src/main_device.zig:41-47) with the head dimensions each one's
+// entry guard lets through (bit 0: 16, bit 1: 32, bit 2: 64) and whether it
+// ignores the causal flag, plus this library's own labels.
+struct KernelAlias {
+    const char *name;
+    uint32_t dims;
+    bool always_causal;
+};
+constexpr KernelAlias kAliases[] = {
+    {"flash_attention_fwd", 7u, false},             // src/kernels.zig:380-394
+    {"flash_attention_fwd_opt", 7u, false},         // src/flash_opt.zig:17-31
+    {"flash_attention_fwd_v2", 7u, false},          // src/flash_v2.zig:23-37
+    {"flash_attention_fwd_h64", 4u, false},         // src/flash_h64.zig:21-35
+    {"flash_attention_fwd_h64_bn32", 4u, false},    // src/flash_h64_bn32.zig:26-40
+    {"flash_attention_fwd_h64_causal", 4u, true},   // src/flash_h64_causal.zig:20-35
+    {"flash_fwd_sm100a_d16", 1u, false},
+    {"flash_fwd_sm100a_d32", 2u, false},
+    {"flash_fwd_sm100a_d64", 4u, false},
+};
+
+const KernelAlias *find_alias(const char *name) {
+    for (const KernelAlias &a : kAliases)
+        if (std::strcmp(a.name, name) == 0) return &a;
+    return nullptr;
+}
+
 // Per-device streams and events of the host-buffer pipeline (library-owned,
 // created on first use).  `mu` serialises callers on one device: the events
 // are re-recorded per chunk and waited on right away, which is only ordered
@@ -717,6 +744,28 @@ int ncz_flash_fwd(const void *q, const void *k, const void *v, void *o, size_t b
     if (st != NCZ_SUCCESS) return st;
     return launch_resolved(reference_args(q, k, v, o, batch_heads, seq_len, head_dim, q_stride, k_stride, v_stride,
                                           o_stride, scale, causal, stream));
+}
+
+int ncz_flash_kernel_info(const char *kernel, uint32_t *head_dims, uint32_t *always_causal) {
+    if (kernel == nullptr) return NCZ_ERROR_INVALID_VALUE;
+    const KernelAlias *a = find_alias(kernel);
+    if (a == nullptr) return NCZ_ERROR_NOT_FOUND;
+    if (head_dims != nullptr) *head_dims = a->dims;
+    if (always_causal != nullptr) *always_causal = a->always_causal ? 1u : 0u;
+    return NCZ_SUCCESS;
+}
+
+int ncz_flash_fwd_named(const char *kernel, const void *q, const void *k, const void *v, void *o,
+                        size_t batch_heads, size_t seq_len, size_t head_dim, size_t q_stride, size_t k_stride,
+                        size_t v_stride, size_t o_stride, float scale, uint32_t causal, void *stream) {
+    if (kernel == nullptr) return NCZ_ERROR_INVALID_VALUE;
+    const KernelAlias *a = find_alias(kernel);
+    if (a == nullptr) return NCZ_ERROR_NOT_FOUND;
+    if (batch_heads == 0) return NCZ_ERROR_INVALID_VALUE;
+    const uint32_t bit = head_dim == 16 ? 1u : head_dim == 32 ? 2u : head_dim == 64 ? 4u : 0u;
+    if (seq_len == 0 || (a->dims & bit) == 0) return NCZ_SUCCESS;  // the kernel's entry guard returns
+    return ncz_flash_fwd(q, k, v, o, batch_heads, seq_len, head_dim, q_stride, k_stride, v_stride, o_stride, scale,
+                         a->always_causal ? 1u : causal, stream);
 }
 
 int ncz_flash_launch(const void *q, size_t q_len, const void *k, size_t k_len, const void *v, size_t v_len, void *o,

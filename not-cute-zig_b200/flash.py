@@ -107,6 +107,12 @@ _SIGNATURES = {
         [_VP, _SZ, _VP, _SZ, _VP, _SZ, _VP, _SZ] + [_SZ] * 7 + [ctypes.c_float, ctypes.c_uint32, _VP],
     ),
     "ncz_flash_fwd_ex": (ctypes.c_int, [ctypes.POINTER(_Desc)]),
+    "ncz_flash_fwd_named": (
+        ctypes.c_int,
+        [ctypes.c_char_p, _VP, _VP, _VP, _VP] + [_SZ] * 7 + [ctypes.c_float, ctypes.c_uint32, _VP],
+    ),
+    "ncz_flash_kernel_info": (ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint32),
+                                             ctypes.POINTER(ctypes.c_uint32)]),
     "ncz_flash_fwd_multi": (ctypes.c_int, [ctypes.POINTER(_Desc), ctypes.c_int]),
     "ncz_flash_fwd_host": (ctypes.c_int, [ctypes.POINTER(_Desc), _VP, _VP, _VP, _VP, _SZ]),
     "ncz_flash_fwd_splits": (ctypes.c_int, [ctypes.POINTER(_Desc), ctypes.c_int]),
@@ -243,6 +249,47 @@ def launch(q, k, v, o, opts: Options, stream=None) -> None:
             float(opts.scale), int(bool(opts.causal)), _stream_handle(stream),
         )
     _check(status, "flash.launch")
+
+
+# The reference's exported flash kernels (src/main_device.zig:41-47), all
+# accepted by launch_named, as are the labels select_kernel returns.
+REFERENCE_KERNELS = (
+    "flash_attention_fwd", "flash_attention_fwd_opt", "flash_attention_fwd_v2", "flash_attention_fwd_h64",
+    "flash_attention_fwd_h64_bn32", "flash_attention_fwd_h64_causal",
+)
+
+
+def kernel_info(name: str):
+    """(head dims the kernel name accepts, always causal) for a name
+    launch_named accepts; FlashError(NotFound) for any other."""
+    dims, causal = ctypes.c_uint32(0), ctypes.c_uint32(0)
+    _check(lib().ncz_flash_kernel_info(name.encode(), ctypes.byref(dims), ctypes.byref(causal)), f"kernel {name!r}")
+    return tuple(d for bit, d in ((1, 16), (2, 32), (4, 64)) if dims.value & bit), bool(causal.value)
+
+
+def launch_named(kernel: str, q, k, v, o, opts: Options, stream=None) -> None:
+    """module.getFunction(kernel) + Function.launch with the 12-argument tuple
+    and grid.y = batch_heads (src/main.zig:93-94, :820-852): `kernel` is one of
+    REFERENCE_KERNELS or a select_kernel label.  As the named kernel does, a
+    head_dim it does not take (the h64 kernels take 64 only) or seq_len 0
+    returns without writing O; flash_attention_fwd_h64_causal is causal
+    whatever opts.causal says.  Unknown names raise FlashError(NotFound)."""
+    import torch
+
+    _require(q, "float16", "q")
+    _require(k, "float16", "k")
+    _require(v, "float16", "v")
+    _require(o, "float32", "o")
+    if not (k.device == v.device == o.device == q.device):
+        raise FlashError(5, "q, k, v and o must be on one device")
+    with torch.cuda.device(q.device):
+        status = lib().ncz_flash_fwd_named(
+            kernel.encode(), q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+            opts.batch_heads, opts.seq_len, opts.head_dim,
+            opts.q_stride, opts.k_stride, opts.v_stride, opts.o_stride,
+            float(opts.scale), int(bool(opts.causal)), _stream_handle(stream),
+        )
+    _check(status, f"launch_named({kernel})")
 
 
 def make_desc(q, k, v, o, opts: Options, *, row_strides: Optional[Sequence[int]] = None,

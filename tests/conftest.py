@@ -25,3 +25,18 @@ def oracle_mod():
     import oracle
 
     return oracle
+
+
+@pytest.fixture
+def fake(ncz):
+    """The library's driver-call table swapped for eight fake devices
+    (tests/fake_driver.py) for one test; on the way out the CUDA runtime is
+    restored and nothing the library made may be left alive."""
+    from tests import fake_driver
+
+    f = fake_driver.FakeDevices(8)
+    assert ncz.driver.install(f.table()) == 0
+    yield f
+    ncz.driver.install(None)
+    assert f.live() == {"streams": 0, "events": 0, "pools": 0, "allocs": 0}
+    assert f.errors == []

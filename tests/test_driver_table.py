@@ -53,16 +53,6 @@ def split_plan(ncz, bh, seq):
     return out[0]
 
 
-@pytest.fixture
-def fake(ncz):
-    f = F.FakeDevices(8)
-    assert ncz.driver.install(f.table()) == 0
-    yield f
-    ncz.driver.install(None)
-    assert f.live() == {"streams": 0, "events": 0, "pools": 0, "allocs": 0}
-    assert f.errors == []
-
-
 def test_table_layout_and_rejected_tables(ncz):
     lib = ncz.driver.lib()
     assert ctypes.sizeof(ncz.driver.DriverTable) == ctypes.sizeof(ctypes.c_size_t) + 24 * ctypes.sizeof(

@@ -412,6 +412,45 @@ def test_expired_wait_reports_device_timeout_and_context_survives(ncz, oracle_mo
     C.check(got, C.reference(p, oracle_mod), C.active_index(p), "launch after an expired wait")
 
 
+def test_reference_kernel_names(ncz):
+    """launch_named with the reference's kernel names: the same bits as
+    flash.launch for every name that takes the head_dim; h64_causal is causal
+    with the flag off; a head_dim the name does not take leaves O untouched."""
+    dev = torch.device("cuda:0")
+    g = torch.Generator(device=dev)
+    g.manual_seed(11)
+
+    def problem(bh, s, d):
+        q, k, v = (torch.randn(bh * s * d, generator=g, device=dev).half() for _ in range(3))
+        return q, k, v, ncz.Options(seq_len=s, head_dim=d, q_stride=s * d, k_stride=s * d, v_stride=s * d,
+                                    o_stride=s * d, scale=1.0 / math.sqrt(d), batch_heads=bh, causal=True)
+
+    for d in (16, 32, 64):
+        q, k, v, opts = problem(3, 700, d)
+        want = torch.zeros(q.numel(), dtype=torch.float32, device=dev)
+        ncz.launch(q, k, v, want, opts)
+        for name in ncz.flash.REFERENCE_KERNELS:
+            dims, always_causal = ncz.flash.kernel_info(name)
+            o = torch.full_like(want, 7.0)
+            ncz.launch_named(name, q, k, v, o, opts)
+            torch.cuda.synchronize()
+            if d in dims:
+                assert torch.equal(o, want), (name, d)
+            else:
+                assert bool((o == 7.0).all()), (name, d)
+    q, k, v, opts = problem(2, 513, 64)
+    want = torch.zeros(q.numel(), dtype=torch.float32, device=dev)
+    ncz.launch(q, k, v, want, opts)
+    opts.causal = False
+    o = torch.zeros_like(want)
+    ncz.launch_named("flash_attention_fwd_h64_causal", q, k, v, o, opts)
+    other = torch.zeros_like(want)
+    ncz.launch_named("flash_attention_fwd_h64_bn32", q, k, v, other, opts)
+    torch.cuda.synchronize()
+    assert torch.equal(o, want) and not torch.equal(other, want)
+    assert ncz.sync_status() == 0
+
+
 def test_compare_harness_records(ncz):
     """compare.py (the reference's compareFlash + JSONL record) on three of the
     reference shapes: correct against fp32 torch attention, rates consistent."""
