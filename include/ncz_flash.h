@@ -169,13 +169,28 @@ int ncz_flash_fwd_ex(const ncz_flash_desc *desc);
  * (ceil(S/16), bh), src/flash.zig:45-69). */
 int ncz_flash_fwd_splits(const ncz_flash_desc *desc, int splits);
 
-/* ncz_flash_fwd_splits without any allocation: split-KV partials go to a
- * static 16 MiB scratch array of the library's device image (one per device)
- * instead of the memory pool.  The split count is lowered until the partials
- * (splits x batch_heads x seq_len x (head_dim + 2) floats) fit, down to no
- * split.  The array is shared by all such launches on a device, so they must
- * be ordered (one stream, or event-ordered streams); ncz_flash_fwd_splits has
- * no such restriction. */
+/* Bytes of the fixed split-KV scratch that ncz_flash_fwd_static uses on each
+ * device (held from library load until the process exits). */
+#define NCZ_STATIC_SCRATCH_BYTES (16u << 20)
+
+/* ncz_flash_fwd_splits for callers that must not let this library allocate
+ * device memory: hosts whose own allocator owns every device buffer (as the
+ * reference's Zig host does with cuda.malloc), and request loops that cannot
+ * afford an allocation that may block, or fail mid-request when memory is
+ * tight.  No counterpart in the reference, whose kernels need no scratch.
+ *
+ * The split-KV partials (splits x batch_heads x seq_len x (head_dim + 2)
+ * floats) go to a fixed array of NCZ_STATIC_SCRATCH_BYTES in the library's
+ * device image instead of the memory pool; nothing is allocated or freed.
+ * splits = 0 (automatic) takes the largest split count whose partials fit,
+ * down to no split.  An explicit splits > 1 whose partials do not fit returns
+ * NCZ_ERROR_OUT_OF_MEMORY before anything is launched.  The first call on a
+ * device looks up the array's device address (device switched to desc->device
+ * for it), so make that first call before any stream capture.  Every call on a
+ * device shares the one array, which keeps the last call's partials (each call
+ * writes every partial it reads, so nothing needs clearing): calls whose
+ * kernels overlap on the GPU race, so order them (one stream, or streams
+ * ordered by events).  ncz_flash_fwd_splits has no such restriction. */
 int ncz_flash_fwd_static(const ncz_flash_desc *desc, int splits);
 
 /* One call, several devices: descs[i] is launched on descs[i].device (each on

@@ -25,6 +25,15 @@
 #include "status.cuh"
 #include "ncz_flash.h"
 
+// Split-KV partials of ncz_flash_fwd_static, the entry point that allocates
+// nothing: a fixed array in the library's device image, NCZ_STATIC_SCRATCH_BYTES
+// (16 MiB) on every device that loads the library, held until the process
+// exits.  Host code must not pass `g_ncz_scratch` itself to a kernel (on the
+// host it names a stand-in, not device memory); static_scratch() looks up its
+// device address once per device, with that device current.
+constexpr size_t kStaticScratchFloats = NCZ_STATIC_SCRATCH_BYTES / sizeof(float);
+static __device__ __align__(256) float g_ncz_scratch[kStaticScratchFloats];
+
 namespace {
 
 using ncz::FlashParams;
@@ -208,10 +217,8 @@ int launch_combine(const FlashParams &p, cudaStream_t stream) {
     return NCZ_SUCCESS;
 }
 
-// Static split-KV scratch for ncz_flash_fwd_static: part of the module image,
-// so that entry point allocates nothing.  4 Mi floats = 16 MiB per device.
-constexpr size_t kStaticScratchFloats = size_t(4) << 20;
-__device__ float g_ncz_scratch[kStaticScratchFloats];
+// Device address of g_ncz_scratch per device (set up by the first
+// ncz_flash_fwd_static call on that device, which must be current).
 float *g_scratch_addr[kMaxDevices];
 
 int static_scratch(int dev, float **out) {
@@ -342,10 +349,12 @@ int launch_on_current(const Resolved &r, int dev) {
     p.o_vec = aligned(r.o, 16) && r.os % vec_elems == 0 && r.orow % vec_elems == 0;
     choose_splits(r, dev, &p.num_splits, &p.kv_per_split);
     if (r.scratch != nullptr) {
-        // Fixed scratch: the largest split count (<= the choice) whose partials fit.
+        // Fixed scratch: an explicit split count must fit; the automatic choice
+        // is lowered to the largest count (down to no split) whose partials fit.
         const size_t per_split = r.bh * r.seq * (r.d + 2);
         const int n_kv = static_cast<int>((r.seq + ncz::kBlockN - 1) / ncz::kBlockN);
         int fit = static_cast<int>(std::min<size_t>(r.scratch_floats / per_split, size_t(ncz::kMaxSplits)));
+        if (fit < p.num_splits && r.splits != 0) return NCZ_ERROR_OUT_OF_MEMORY;
         if (fit < p.num_splits) {
             const int want = std::max(1, fit);
             p.kv_per_split = (n_kv + want - 1) / want;

@@ -48,6 +48,7 @@ STATUS_NAMES = {
 }
 
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
+STATIC_SCRATCH_BYTES = 16 << 20  # NCZ_STATIC_SCRATCH_BYTES: ncz_flash_fwd_static's fixed scratch per device
 PRODUCERS = {"auto": 0, "tma": 1, "lsu": 2}
 
 
@@ -347,8 +348,14 @@ def launch_splits(q, k, v, o, opts: Options, splits: int, *, row_strides: Option
 
 def launch_static(q, k, v, o, opts: Options, splits: int = 0, *, row_strides: Optional[Sequence[int]] = None,
                   producer: str = "auto", stream=None) -> None:
-    """ncz_flash_fwd_static: launch_splits with the partials in the library's
-    static device scratch (no allocation); launches on one device must be ordered."""
+    """ncz_flash_fwd_static: launch_splits for callers that cannot let the
+    library allocate device memory.  The split-KV partials go to a fixed
+    STATIC_SCRATCH_BYTES array of the library's device image; splits = 0 takes
+    the largest count that fits, an explicit count that does not fit raises
+    FlashError(OutOfMemory) before any launch.  All such calls on a device
+    share the array: order them (one stream or event-ordered streams), and
+    make the first one on a device before any stream capture (it looks up the
+    array's address)."""
     d = make_desc(q, k, v, o, opts, row_strides=row_strides, producer=producer, stream=stream)
     _check(lib().ncz_flash_fwd_static(ctypes.byref(d), int(splits)), "flash.launch_static")
 

@@ -133,6 +133,9 @@ def test_static_scratch_allocates_nothing(ncz, fake):
     assert labels(ncz, fake.launches) == ["flash_fwd<64,tma,f16>", "combine_splits<64>"] * 2
     assert fake.created["alloc"] == 0 and fake.created["pool"] == 0
     assert fake.calls[("symbol_address", 0)] == 1  # resolved once per device
+    # an explicit split count whose partials exceed the 16 MiB scratch: refused before any launch
+    assert status(ncz, lib.ncz_flash_fwd_static(ctypes.byref(x), 8)) == "OutOfMemory"
+    assert len(fake.launches) == 4 and fake.created["alloc"] == 0
 
 
 def test_device_selection_failures(ncz, fake):

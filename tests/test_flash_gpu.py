@@ -367,18 +367,26 @@ def test_static_scratch_entry_matches_pool_path(ncz, oracle_mod):
     C.check(a.cpu().numpy(), C.reference(p, oracle_mod), C.active_index(p), "static scratch bh=1 S=4096")
 
 
-@pytest.mark.parametrize("bh,splits,expect", [(2, 4, 3), (4, 8, 1)])
-def test_static_scratch_lowers_the_split_count_to_fit(ncz, oracle_mod, bh, splits, expect):
+@pytest.mark.parametrize("bh,splits,fits", [(2, 0, 3), (2, 3, 3), (2, 4, 0), (4, 8, 0), (4, 0, 1)])
+def test_static_scratch_split_count_must_fit(ncz, oracle_mod, bh, splits, fits):
     """16 MiB of scratch holds 4 Mi floats: at S=8192, d=64 one split of bh slices
-    needs bh*8192*66 floats, so bh=2 runs 3 splits and bh=4 runs unsplit; the
-    results equal the pool path run with that split count, bit for bit."""
+    needs bh*8192*66 floats.  The automatic count (0) runs what fits (bh=2: 3
+    splits; bh=4: unsplit); an explicit count that fits runs as asked; one that
+    does not raises OutOfMemory and launches nothing.  Results equal the pool
+    path run with the same split count, bit for bit."""
     p = C.normal_problem(bh, 8192, 64, True, 13, oracle_mod, std=0.7)
     q, k, v, opts = _dev_inputs(p)
     a, b = _out(p), _out(p)
     before = ncz.flash.launch_count()
+    if fits == 0:
+        with pytest.raises(ncz.FlashError) as err:
+            ncz.launch_static(q, k, v, a, opts, splits)
+        assert err.value.name == "OutOfMemory" and ncz.flash.launch_count() == before
+        assert bool((a == SENTINEL).all())
+        return
     ncz.launch_static(q, k, v, a, opts, splits)
-    assert ncz.flash.launch_count() - before == (2 if expect > 1 else 1)
-    ncz.launch_splits(q, k, v, b, opts, expect)
+    assert ncz.flash.launch_count() - before == (2 if fits > 1 else 1)
+    ncz.launch_splits(q, k, v, b, opts, fits)
     assert ncz.sync_status() == 0
     assert torch.equal(a, b)
 
