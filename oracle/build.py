@@ -18,7 +18,10 @@ ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_DIR = os.path.join(HERE, "_ref")
 REF_SO = os.path.join(REF_DIR, "libncz_ref.so")
 REF_BIN = os.path.join(REF_DIR, "cuda_baselines")
-REFERENCE_ROOT = os.environ.get("NCZ_REFERENCE_ROOT", "/root/reference")
+# The reference checkout sits beside this repository ("reference/" next to the
+# repository root) unless NCZ_REFERENCE_ROOT names another place.
+REFERENCE_ROOT = os.environ.get("NCZ_REFERENCE_ROOT",
+                                os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
 NVCC = os.environ.get("NVCC", "nvcc")
 
 
