@@ -80,6 +80,11 @@ struct Resolved {
     bool use_static = false;   // split-KV partials in the static scratch array, not the pool
     float *scratch = nullptr;  // (resolved on the launch device)
     size_t scratch_floats = 0;
+#ifdef NCZ_DEBUG_ITEM_VISITS
+    unsigned int *item_visits = nullptr;  // debug build: per-item visit counters (device)
+    size_t item_visits_cap = 0;
+    size_t *items_out = nullptr;
+#endif
 };
 
 bool mul_ok(size_t a, size_t b, size_t *out) { return !__builtin_mul_overflow(a, b, out); }
@@ -383,6 +388,14 @@ int launch_on_current(const Resolved &r, int dev) {
     // not started yet.
     const size_t items = static_cast<size_t>(p.num_groups) * r.bh * static_cast<size_t>(p.num_splits);
     const unsigned grid = static_cast<unsigned>(items);
+#ifdef NCZ_DEBUG_ITEM_VISITS
+    p.item_visits = r.item_visits;
+    if (r.items_out != nullptr) *r.items_out = items;
+    if (r.item_visits != nullptr && items > r.item_visits_cap) {
+        if (ws != nullptr) drv().free_async(ws, r.stream);
+        return NCZ_ERROR_OVERFLOW;
+    }
+#endif
     p.walk_tiles = NCZ_WALK_TILES;
     {
         // NCZ_CHUNK_KV_BYTES of K/V per chunk of slices: with the items in
@@ -927,6 +940,24 @@ int ncz_test_drop_arrive(int device, int enable) {
     const int v = enable != 0;
     return write_symbol(device, static_cast<const void *>(&ncz::g_ncz_test_drop), &v, sizeof(v));
 }
+
+#ifdef NCZ_DEBUG_ITEM_VISITS
+// Debug build only (libncz_flash_debug.so, not part of the public headers):
+// ncz_flash_fwd_splits with a per-item visit counter.  visits is a device
+// array of at least `cap` zeroed uint32 counters; after the launch entry i
+// holds the number of CTAs that started work item i (1 for a correct walk).
+// *items receives the launch's item count; NCZ_ERROR_OVERFLOW (nothing
+// launched) when it exceeds cap.
+int ncz_debug_item_visits(const ncz_flash_desc *desc, int splits, unsigned int *visits, size_t cap, size_t *items) {
+    if (desc == nullptr || splits < 0 || visits == nullptr || items == nullptr) return NCZ_ERROR_INVALID_VALUE;
+    Resolved r = from_desc(*desc);
+    r.splits = splits;
+    r.item_visits = visits;
+    r.item_visits_cap = cap;
+    r.items_out = items;
+    return launch_resolved(r);
+}
+#endif
 
 const char *ncz_status_string(int status) {
     switch (status) {

@@ -144,7 +144,24 @@ struct FlashParams {
     int chunk_slices;
     float *part_o;
     float *part_ml;
+#ifdef NCZ_DEBUG_ITEM_VISITS
+    // Debug build only (libncz_flash_debug.so): when set, item_visits[item]
+    // counts the CTAs whose producer started that work item; a correct walk
+    // leaves exactly 1 in every entry.
+    unsigned int *item_visits;
+#endif
 };
+
+// Debug build only: one count per work item started (producer warp, lane 0).
+__device__ __forceinline__ void count_item_visit(const FlashParams &p, int item, int lane) {
+#ifdef NCZ_DEBUG_ITEM_VISITS
+    if (lane == 0 && p.item_visits != nullptr) atomicAdd(p.item_visits + item, 1u);
+#else
+    (void)p;
+    (void)item;
+    (void)lane;
+#endif
+}
 
 template <int D>
 struct SmemLayout {
@@ -348,6 +365,7 @@ __device__ __forceinline__ void producer_tma(const FlashParams &p, const CUtenso
     bool ok = true;
     for (int item = static_cast<int>(blockIdx.x); ok && item >= 0;) {
         const Work wk = make_work(p, item);
+        count_item_visit(p, item, lane);
         const int qs = it & 1;
         if (it >= 2 && !warp_wait(b.q_empty(qs), ((it >> 1) - 1) & 1, abort_flag, kSiteQEmpty)) {
             ok = false;
@@ -445,6 +463,7 @@ __device__ __forceinline__ void producer_lsu(const FlashParams &p, uint8_t *smem
     bool ok = true;
     for (int item = static_cast<int>(blockIdx.x); ok && item >= 0;) {
         const Work wk = make_work(p, item);
+        count_item_visit(p, item, lane);
         const uint16_t *qs = p.q + wk.slice * p.q_stride;
         const uint16_t *ks = p.k + wk.slice * p.k_stride;
         const uint16_t *vs = p.v + wk.slice * p.v_stride;
