@@ -47,7 +47,13 @@ WORKLOADS = {
     "c2": (8, 1024, 64, True, 0.5, 1.0, 1, "f16", "config2_profile bh=8 S=1024 d=64 causal N(0,.25) f16 O"),
     "c5": (1024, 2048, 64, False, 0.5, 1.0, 4, "f32", "config5_sweep bh=1024 S=2048 d=64 non-causal N(0,.25)"),
     "c5d16": (1024, 2048, 16, False, 0.5, 1.0, 5, "f32", "config5_sweep bh=1024 S=2048 d=16 non-causal N(0,.25)"),
+    "c3": (512, 128, 32, False, None, None, 2, "f32",
+           "config3_padded bh=512 S=128 d=32 non-causal, Q/K/V row stride 40 (NaN padding), U(-1,1)"),
 }
+# Workloads with padded Q/K/V rows (`row` elements apart, NaN in the padding,
+# O contiguous) and U(lo, hi) values; their roofline is HBM bandwidth.
+PADDED = {"c3": {"row": 40, "lo": -1.0, "hi": 1.0}}
+FALLBACK_HBM_GBS = 6650.0
 L2_BYTES = 126 * 1024 * 1024
 
 
@@ -64,6 +70,15 @@ def load_peaks():
         return float(pk["bf16_tflops"]), float(pk["bf16_tflops_sustained"]), "measured"
     except Exception:
         return FALLBACK_TFLOPS, FALLBACK_TFLOPS, "fallback"
+
+
+def load_hbm():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
 
 
 def load_traffic(workload):
@@ -134,6 +149,17 @@ def make_inputs(oracle, bh, s, d, std, k_mul, seed):
 # ---------------------------------------------------------------------------
 # CPU leg: the oracle (restated reference CPU attention) on a bounded sample
 # ---------------------------------------------------------------------------
+def make_padded_inputs(oracle, bh, s, d, row, lo, hi, seed):
+    """Q, K, V of bh slices of s rows `row` elements apart: U(lo, hi) values
+    (seeds seed*3 + 0..2), NaN in each row's padding columns."""
+    out = []
+    for i in range(3):
+        a = oracle.fill_uniform(bh * s * row, seed * 3 + i, lo, hi)
+        oracle.fill_row_padding(a, bh, s, d, s * row, row)
+        out.append(a)
+    return out
+
+
 def host_threads(oracle):
     """All host threads this process may run on (torchrun sets OMP_NUM_THREADS=1
     for its workers; the CPU legs use every core they are allowed)."""
@@ -226,7 +252,12 @@ def reference_arm(args):
     import oracle
 
     bh, s, d, causal, std, k_mul, seed, o_dtype, desc = WORKLOADS[args.workload]
-    q, k, v = make_inputs(oracle, 1, s, d, std, k_mul, seed)
+    pad = PADDED.get(args.workload)
+    if pad:  # the oracle reads the same values with the padding removed
+        q, k, v = (a.reshape(s, pad["row"])[:, :d].reshape(-1).copy()
+                   for a in make_padded_inputs(oracle, 1, s, d, pad["row"], pad["lo"], pad["hi"], seed))
+    else:
+        q, k, v = make_inputs(oracle, 1, s, d, std, k_mul, seed)
     scale = 1.0 / math.sqrt(d)
     threads = host_threads(oracle)
     budget = 90.0  # seconds of CPU work for the whole --steps/--warmup run
@@ -317,19 +348,26 @@ def main():
     bh, s, d, causal, std, k_mul, seed, o_dtype, desc = WORKLOADS[args.workload]
     scale = 1.0 / math.sqrt(d)
     n = bh * s * d
+    pad = PADDED.get(args.workload)
+    row = pad["row"] if pad else d
+    n_in = bh * s * row  # elements of each of Q, K, V (padding included)
+    row_strides = (row, row, row, d) if pad else None
     # Weak scaling: every rank owns its own bh slices (seeded by rank).
-    hq, hk, hv = make_inputs(oracle, bh, s, d, std, k_mul, seed + 1000 * rank)
+    if pad:
+        hq, hk, hv = make_padded_inputs(oracle, bh, s, d, row, pad["lo"], pad["hi"], seed + 1000 * rank)
+    else:
+        hq, hk, hv = make_inputs(oracle, bh, s, d, std, k_mul, seed + 1000 * rank)
     q = torch.from_numpy(hq).to(dev)
     k = torch.from_numpy(hk).to(dev)
     v = torch.from_numpy(hv).to(dev)
     tdt = torch.float16 if o_dtype == "f16" else torch.float32
     o = torch.empty(n, dtype=tdt, device=dev)
-    working_set = 3 * n * 2 + n * o.element_size()
+    working_set = 3 * n_in * 2 + n * o.element_size()
     # Inputs + O smaller than L2: flush L2 before every timed step (memset of a
     # 256 MB buffer, outside the timed intervals).
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev) if working_set <= L2_BYTES else None
-    opts = ncz.Options(seq_len=s, head_dim=d, q_stride=s * d, k_stride=s * d, v_stride=s * d, o_stride=s * d,
-                       scale=scale, batch_heads=bh, causal=causal)
+    opts = ncz.Options(seq_len=s, head_dim=d, q_stride=s * row, k_stride=s * row, v_stride=s * row,
+                       o_stride=s * d, scale=scale, batch_heads=bh, causal=causal)
     stream = torch.cuda.current_stream(dev)
     step_flops = flops_of(bh, s, d, causal)
 
@@ -340,9 +378,9 @@ def main():
 
     def step():
         if args.splits is not None:
-            ncz.launch_splits(q, k, v, o, opts, args.splits, stream=stream)
-        elif o_dtype == "f16":
-            ncz.launch_ex(q, k, v, o, opts, stream=stream)
+            ncz.launch_splits(q, k, v, o, opts, args.splits, row_strides=row_strides, stream=stream)
+        elif o_dtype == "f16" or pad:
+            ncz.launch_ex(q, k, v, o, opts, row_strides=row_strides, stream=stream)
         else:
             ncz.launch(q, k, v, o, opts, stream=stream)
 
@@ -392,7 +430,7 @@ def main():
         dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
 
         def e2e_step():
-            ncz.launch_host(pq, pk_, pv, po, dq, dk, dv, o, opts, stream=stream)
+            ncz.launch_host(pq, pk_, pv, po, dq, dk, dv, o, opts, row_strides=row_strides, stream=stream)
 
         for _ in range(3):
             e2e_step()
@@ -407,7 +445,7 @@ def main():
         if dist is not None:
             dist.all_reduce(et, op=dist.ReduceOp.MAX)
         e2e = {"value": world * step_flops * args.e2e_steps / (float(et.item()) / 1e3) / 1e12, "unit": "TFLOP/s",
-               "h2d_bytes_per_step": 3 * n * 2, "d2h_bytes_per_step": n * o.element_size(), "steps": args.e2e_steps,
+               "h2d_bytes_per_step": 3 * n_in * 2, "d2h_bytes_per_step": n * o.element_size(), "steps": args.e2e_steps,
                "api": "flash.launch_host -> ncz_flash_fwd_host (C ABI), default chunking"}
 
     # Optional O gather to rank 0 over NVLink (NCCL), off the timed metric.
@@ -434,7 +472,8 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        tf, dt, what, fl, thr, _ = cpu_sample(oracle, hq, hk, hv, s, d, causal, scale, args.cpu_seconds, bh=bh)
+        cq, ck, cv = (a.reshape(bh, s, row)[:, :, :d].reshape(-1).copy() for a in (hq, hk, hv)) if pad else (hq, hk, hv)
+        tf, dt, what, fl, thr, _ = cpu_sample(oracle, cq, ck, cv, s, d, causal, scale, args.cpu_seconds, bh=bh)
         cpu = {"value": tf, "unit": "TFLOP/s", "cores": thr, "kind": "port",
                "sample": f"oracle (restatement of src/main.zig:1271-1307) on {what} "
                          f"({fl / 1e9:.2f} GFLOP in {dt:.1f} s), {cpu_model()}"}
@@ -446,6 +485,19 @@ def main():
         timed_s = ms_max / 1e3
         peak = sustained if timed_s > 1.0 else burst
         traffic = load_traffic(args.workload)
+        if pad:
+            # HBM-bound: algorithmic bytes by the reference formula
+            # (bh*S*d*(3*2 + O bytes), src/main.zig:845) per launch over its time.
+            hbm, hsrc = load_hbm()
+            gbs = n * (3 * 2 + o.element_size()) / (ms_step / 1e3) / 1e9
+            roofline = {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s", "frac": gbs / hbm,
+                        "traffic": traffic, "peak_source": f"{hsrc} HBM copy",
+                        "kernel": f"ncz::flash_fwd_sm100<{d},true,false>"}
+        else:
+            roofline = {"bound": "tensor", "achieved": per_gpu, "peak": peak, "unit": "TFLOP/s",
+                        "frac": per_gpu / peak, "traffic": traffic,
+                        "peak_source": f"{src} bf16 {'sustained' if peak == sustained else 'burst'}",
+                        "kernel": f"ncz::flash_fwd_sm100<{d},true,false>"}
         line = {
             "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
@@ -455,13 +507,10 @@ def main():
                        "parallelism": f"slices sharded x{world}, no collective", "split_kv": "auto" if args.splits is None else args.splits,
                        "l2": ("inputs 3x%.1f MB + O %.1f MB > 126 MB L2; no flush" if flush is None else
                               "inputs 3x%.1f MB + O %.1f MB fit in L2: 256 MB memset before every timed step, "
-                              "outside the timed intervals") % (n * 2 / 1e6, n * o.element_size() / 1e6)},
+                              "outside the timed intervals") % (n_in * 2 / 1e6, n * o.element_size() / 1e6)},
             "pct_peak_nominal": per_gpu / NOMINAL_F16_TFLOPS,
             "pct_peak_measured": per_gpu / peak,
-            "roofline": {"bound": "tensor", "achieved": per_gpu, "peak": peak, "unit": "TFLOP/s",
-                         "frac": per_gpu / peak, "traffic": traffic,
-                         "peak_source": f"{src} bf16 {'sustained' if peak == sustained else 'burst'}",
-                         "kernel": f"ncz::flash_fwd_sm100<{d},true,false>"},
+            "roofline": roofline,
             "cpu_baseline": cpu,
             "e2e": e2e,
             "o_gather": gather,
