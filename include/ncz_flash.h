@@ -90,7 +90,13 @@ typedef struct ncz_flash_desc {
 /* Loads nothing eagerly; resolves the driver entry points and records the
  * device count.  Idempotent.  Called implicitly by every launch. */
 int ncz_init(void);
-/* Drops cached per-device state.  Kernels in flight are not waited for. */
+/* Releases what the library owns on every device (split-KV memory pools,
+ * host-pipeline streams and events) and drops its cached per-device state
+ * (initialisation, kernel attributes, tensor maps, SM counts); the next call
+ * initialises again.  Kernels and copies in flight are not waited for: the
+ * runtime frees a stream or pool once its work is done.  Returns the first
+ * error of the release, else NCZ_SUCCESS.  No other thread may be inside the
+ * library meanwhile. */
 int ncz_shutdown(void);
 
 /* flash.Options.validate (src/flash.zig:16-28): batch_heads > 0, seq_len > 0,

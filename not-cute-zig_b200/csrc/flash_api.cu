@@ -719,12 +719,10 @@ int ncz_init(void) {
 }
 
 int ncz_shutdown(void) {
-    std::lock_guard<std::mutex> lock(g_mu);
-    std::memset(g_attr_done, 0, sizeof(g_attr_done));
-    for (MapSlot &m : g_maps) m.used = false;
-    g_init_done = false;
-    g_init_status = NCZ_ERROR_NOT_INITIALIZED;
-    return NCZ_SUCCESS;
+    const int released = ncz::release_flash_objects();
+    ncz::reset_flash_caches();
+    ncz::reset_mma_caches();
+    return released;
 }
 
 int ncz_flash_validate(size_t batch_heads, size_t seq_len, size_t head_dim, size_t q_stride, size_t k_stride,

@@ -290,6 +290,21 @@ def test_switching_tables_releases_through_the_old_one(ncz, fake):
     assert ncz.driver.install(None) == 0 and other.errors == []
 
 
+def test_shutdown_releases_everything_and_the_next_call_starts_over(ncz, fake):
+    lib = ncz.flash.lib()
+    assert fwd_host(ncz, desc(ncz, 2, bh=8), 0) == 0
+    assert fwd(ncz, desc(ncz, 6, bh=1, seq=8192, base=BASE + SPAN)) == 0
+    assert fake.live() == {"streams": 2, "events": 4, "pools": 1, "allocs": 0}
+    assert lib.ncz_shutdown() == 0
+    assert fake.live() == {"streams": 0, "events": 0, "pools": 0, "allocs": 0}
+    counted = fake.calls[("get_device_count", 0)]
+    assert fwd(ncz, desc(ncz, 0)) == 0  # initialised again
+    assert fake.calls[("get_device_count", 0)] == counted + 1
+    fake.fail("pool_destroy", error=F.ILLEGAL_ADDRESS)
+    assert fwd(ncz, desc(ncz, 6, bh=1, seq=8192, base=BASE + SPAN)) == 0
+    assert status(ncz, lib.ncz_shutdown()) == "IllegalAddress" and fake.live()["pools"] == 0
+
+
 def test_release_error_is_reported_and_the_rest_released(ncz, fake):
     before = F.FakeDevices()  # a table to go back to after the failing release
     assert fwd_host(ncz, desc(ncz, 1, bh=8), 0) == 0
