@@ -25,7 +25,13 @@ def work(lib, bh, s, causal, splits, chunk, i):
     (5, 100, True, 1, 5),      # one group
 ])
 def test_item_order(ncz, bh, s, causal, splits, chunk):
-    lib = ncz.flash.lib()
+    check_item_order(ncz.flash.lib(), bh, s, causal, splits, chunk)
+
+
+def check_item_order(lib, bh, s, causal, splits, chunk):
+    """Every (slice, Q group, K range) once, chunks in order, heaviest group
+    first inside a chunk, each Q tile's K tiles inside its range and causal
+    bound; one item past the end is refused."""
     groups = math.ceil(s / 256)
     n_kv = math.ceil(s / 128)
     ns = work(lib, bh, s, causal, splits, chunk, 0)[7]
