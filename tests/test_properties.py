@@ -115,3 +115,40 @@ def test_validate_ex_matches_the_row_stride_rule(ncz, args):
        chunk=st.integers(1, 30))
 def test_item_order_is_a_permutation_for_random_shapes(ncz, bh, s, causal, splits, chunk):
     check_item_order(ncz.flash.lib(), bh, s, causal, splits, chunk)
+
+
+def ref_gemm(ptrs_ok, k_iters, batches, strides):
+    """ncz_mma_matmul_pipelined's argument rule: zero batches launch nothing;
+    otherwise every pointer and k_iters >= 1 are required, and k_iters <= 2^24,
+    batches and strides <= 2^40 (64-bit element offsets stay exact)."""
+    if batches == 0:
+        return "Success", 0
+    if not ptrs_ok or k_iters == 0:
+        return "InvalidValue", 0
+    if k_iters > 1 << 24 or batches > 1 << 40 or max(strides) > 1 << 40:
+        return "Overflow", 0
+    return "Success", 1
+
+
+@settings(max_examples=300, deadline=None,
+          suppress_health_check=[hypothesis.HealthCheck.function_scoped_fixture])
+@given(ptrs_ok=st.booleans(), k_iters=st.one_of(st.integers(0, 40), st.sampled_from([1 << 24, (1 << 24) + 1, U64])),
+       batches=st.one_of(st.integers(0, 100000), st.sampled_from([1 << 40, (1 << 40) + 1, U64])),
+       strides=st.lists(st.one_of(st.integers(0, 4096), st.sampled_from([1 << 40, (1 << 40) + 1])), min_size=3,
+                        max_size=3),
+       epilogue=st.integers(0, 7))
+def test_gemm_arguments_and_launch_shape(ncz, fake, ptrs_ok, k_iters, batches, strides, epilogue):
+    """Under the fake devices: the status follows the rule, and a valid call
+    launches one mma_gemm<row_b> of min(ceil(batches / 8), 2 x SMs) CTAs."""
+    lib = ncz.mma.lib()
+    before = len(fake.launches)
+    ptr = 0x1000_0000 if ptrs_ok else None
+    st_ = lib.ncz_mma_matmul_pipelined(0x1000_0000, ptr, 0x3000_0000, 0x4000_0000, 1.0, 0.5, *strides, k_iters,
+                                       epilogue, batches, None)
+    want, launches = ref_gemm(ptrs_ok, k_iters, batches, strides)
+    assert ncz.flash.STATUS_NAMES[st_] == want
+    new = fake.launches[before:]
+    assert len(new) == launches
+    if launches:
+        assert new[0].grid == min(-(-batches // 8), 2 * fake.sms) and new[0].block == 256
+        assert ncz.driver.kernel_label(new[0].kernel) == "mma_gemm<row_b>"
