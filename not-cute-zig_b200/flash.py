@@ -394,6 +394,13 @@ def sync_status(device: Optional[int] = None, stream=None) -> int:
     return detail.value
 
 
+def shutdown() -> int:
+    """ncz_shutdown: releases the library's pools, streams and events on every
+    device and drops its caches (the next call initialises again); returns
+    the first release error (0 = none).  Work in flight is not waited for."""
+    return int(lib().ncz_shutdown())
+
+
 def launch_count() -> int:
     """Kernel launches issued by this library in this process."""
     return int(lib().ncz_launch_count())

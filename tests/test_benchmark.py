@@ -55,3 +55,22 @@ def test_reference_shape_list(compare):
     from tests import cases as C
 
     assert compare.REFERENCE_SHAPES == C.COMPARE_CASES
+
+
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("row", [0, 40])
+def test_compare_cross_check_agrees_with_the_oracle(compare, oracle_mod, causal, row):
+    """compare.py judges correctness against its own fp32 torch attention; on the
+    CPU that reference must agree with the oracle (float32 rounding only), also
+    with padded rows (--row-stride)."""
+    torch = pytest.importorskip("torch")
+    bh, s, d = 3, 77, 32
+    r = row or d
+    rng = np.random.default_rng(5)
+    q, k, v = (rng.standard_normal(bh * s * r).astype(np.float16) for _ in range(3))
+    scale = d ** -0.5
+    got = compare.torch_attention(*(torch.from_numpy(a) for a in (q, k, v)), bh, s, d, scale, causal, row).numpy()
+    want = oracle_mod.flash_reference(q, k, v, batch_heads=bh, seq_len=s, head_dim=d, q_stride=s * r, k_stride=s * r,
+                                      v_stride=s * r, o_stride=s * d, scale=scale, causal=causal,
+                                      row_strides=(r, r, r, d))
+    assert np.allclose(got, want, atol=2e-5, rtol=1e-4), float(np.abs(got - want).max())
