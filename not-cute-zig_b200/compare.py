@@ -6,7 +6,8 @@ Mirrors compareFlash (src/main.zig:975-1041) and benchmarkFlash
 bytes and FLOPs by the reference formulas (src/main.zig:843-845), and one
 JSONL record per shape in the reference's field order (src/main.zig:873-881)
 plus gpus, device_ms, pct_peak_nominal, pct_peak_measured, max_rel_error,
-host_cores and label.  Correctness is checked against plain fp32 attention in
+host_cores, cpu_ms (with --cpu-ms: the same fp32 attention timed on the host
+CPU) and label.  Correctness is checked against plain fp32 attention in
 torch on the same device (max-abs <= 0.02, the reference's compare bound,
 src/main.zig:1042); rel = |a - b| / max(|b|, 1e-3).
 
@@ -61,6 +62,17 @@ def torch_attention(q, k, v, bh: int, s: int, d: int, scale: float, causal: bool
     return torch.matmul(torch.softmax(scores, dim=-1), vf).reshape(-1)
 
 
+def host_reference_ms(q, k, v, bh: int, s: int, d: int, scale: float, causal: bool, row: int = 0) -> float:
+    """Wall time (ms) of the fp32 cross-check attention computed on the host
+    CPU with torch's threads: the cpu_ms field of a record."""
+    import time
+
+    qc, kc, vc = (t.detach().cpu() for t in (q, k, v))
+    t0 = time.perf_counter()
+    torch_attention(qc, kc, vc, bh, s, d, scale, causal, row)
+    return (time.perf_counter() - t0) * 1e3
+
+
 def measured_peak() -> Optional[float]:
     path = os.path.join(os.path.dirname(_HERE), "MEASURED_PEAKS.json")
     try:
@@ -75,7 +87,7 @@ O_DTYPES = {"f32": ("float32", 4), "f16": ("float16", 2), "bf16": ("bfloat16", 2
 
 
 def compare_shape(ncz, bh: int, s: int, d: int, causal: bool, gpus: int = 1, *, seed: Optional[int] = None,
-                  in_dtype: str = "f16", o_dtype: str = "f32", row_stride: int = 0) -> dict:
+                  in_dtype: str = "f16", o_dtype: str = "f32", row_stride: int = 0, cpu_ms: bool = False) -> dict:
     """One compareFlash record.  Defaults are the reference's: fillFlashInput
     inputs, f16 Q/K/V, f32 O, rows of head_dim elements, through flash.launch.
     `seed` draws N(0, 1) inputs instead; `in_dtype` / `o_dtype` / `row_stride`
@@ -131,6 +143,7 @@ def compare_shape(ncz, bh: int, s: int, d: int, causal: bool, gpus: int = 1, *, 
         res = bench.run_multi(launches, streams, warmup_iters=5, iters=20, bytes_processed=bytes_,
                               flops_processed=flops)
     max_abs, max_rel, padding_kept = 0.0, 0.0, True
+    cpu_total = 0.0 if cpu_ms else None
     for (q, k, v, o, lo, hi), st in zip(outs, streams):
         st.synchronize()
         ncz.sync_status(device=q.device.index, stream=st)
@@ -140,6 +153,8 @@ def compare_shape(ncz, bh: int, s: int, d: int, causal: bool, gpus: int = 1, *, 
         max_abs = max(max_abs, float(diff.max()))
         max_rel = max(max_rel, float((diff / want.abs().clamp_min(1e-3)).max()))
         padding_kept = padding_kept and bool((got[:, :, d:] == 0).all())
+        if cpu_ms:
+            cpu_total += host_reference_ms(q, k, v, hi - lo, s, d, scale, causal, row)
     peak = measured_peak()
     shape = f"batch_heads={bh},seq={s},head={d},causal={str(causal).lower()}"
     if extended:
@@ -154,7 +169,7 @@ def compare_shape(ncz, bh: int, s: int, d: int, causal: bool, gpus: int = 1, *, 
                       gpus=gpus, device_ms=res.device_ms, host_ms=res.host_ms,
                       pct_peak_nominal=(res.tflops or 0.0) / NOMINAL_F16_TFLOPS,
                       pct_peak_measured=((res.tflops or 0.0) / peak) if peak else None,
-                      max_rel_error=max_rel, host_cores=bench.host_cores(), label=label)
+                      max_rel_error=max_rel, host_cores=bench.host_cores(), cpu_ms=cpu_total, label=label)
 
 
 def measured_hbm() -> Optional[float]:
@@ -242,6 +257,8 @@ def main(argv=None) -> int:
     ap.add_argument("--o-dtype", choices=sorted(O_DTYPES), default="f32", help="O element type")
     ap.add_argument("--row-stride", type=int, default=0,
                     help="elements between rows of Q/K/V/O (>= head_dim; 0 = head_dim)")
+    ap.add_argument("--cpu-ms", action="store_true",
+                    help="also time the fp32 cross-check attention on the host CPU (cpu_ms)")
     ap.add_argument("--jsonl", default=None, help="append records to this file instead of stdout")
     ap.add_argument("--mma", action="store_true",
                     help="the GEMM + epilogue records instead: compareMma's 16x8x16 and batched throughput shapes")
@@ -262,7 +279,8 @@ def main(argv=None) -> int:
             bh, s, d, c = (int(x) for x in spec.split(","))
             shapes.append((bh, s, d, bool(c)))
     records = [compare_shape(ncz, bh, s, d, c, args.gpus, seed=args.seed, in_dtype=args.in_dtype,
-                             o_dtype=args.o_dtype, row_stride=args.row_stride) for bh, s, d, c in shapes]
+                             o_dtype=args.o_dtype, row_stride=args.row_stride, cpu_ms=args.cpu_ms)
+               for bh, s, d, c in shapes]
     bench.emit(records, args.jsonl)
     return 0 if all(r["correct"] for r in records) else 1
 

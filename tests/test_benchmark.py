@@ -74,3 +74,11 @@ def test_compare_cross_check_agrees_with_the_oracle(compare, oracle_mod, causal,
                                       v_stride=s * r, o_stride=s * d, scale=scale, causal=causal,
                                       row_strides=(r, r, r, d))
     assert np.allclose(got, want, atol=2e-5, rtol=1e-4), float(np.abs(got - want).max())
+
+
+def test_host_reference_time(compare):
+    """cpu_ms: the cross-check attention timed on the host CPU."""
+    torch = pytest.importorskip("torch")
+    q, k, v = (torch.randn(2 * 64 * 32).half() for _ in range(3))
+    ms = compare.host_reference_ms(q, k, v, 2, 64, 32, 32 ** -0.5, True)
+    assert 0.0 < ms < 60_000.0
