@@ -215,7 +215,12 @@ int ncz_flash_fwd_multi(const ncz_flash_desc *descs, int count);
  * streams, so the upload of chunk i+1 overlaps the forward of chunk i and the
  * download of chunk i-1.  Host buffers must be page-locked (pinned) for the
  * copies to run asynchronously.  Everything is ordered on desc->stream: work
- * enqueued on it afterwards runs once O is in host memory.  Replaces the
+ * enqueued on it afterwards runs once O is in host memory.  Each chunk of O
+ * comes back as one contiguous range, from its first slice's first element to
+ * its last slice's last active element: where O has padding (o_row_stride >
+ * head_dim, or slices more than a slice apart) the host padding inside that
+ * range receives whatever the device O buffer holds there, which the kernel
+ * never writes.  The device entry points leave O padding untouched.  Replaces the
  * upload / flash.launch / download sequence of the reference's callers
  * (src/main.zig:254-271). */
 int ncz_flash_fwd_host(const ncz_flash_desc *desc, const void *q_host, const void *k_host,

@@ -359,7 +359,9 @@ int launch_on_current(const Resolved &r, int dev) {
         const size_t per_split = r.bh * r.seq * (r.d + 2);
         const int n_kv = static_cast<int>((r.seq + ncz::kBlockN - 1) / ncz::kBlockN);
         int fit = static_cast<int>(std::min<size_t>(r.scratch_floats / per_split, size_t(ncz::kMaxSplits)));
-        if (fit < p.num_splits && r.splits != 0) return NCZ_ERROR_OUT_OF_MEMORY;
+        // Without a split nothing goes to the scratch, so only a count that
+        // does split has to fit (an explicit 1, or one the plan clamps to 1, runs).
+        if (p.num_splits > 1 && fit < p.num_splits && r.splits != 0) return NCZ_ERROR_OUT_OF_MEMORY;
         if (fit < p.num_splits) {
             const int want = std::max(1, fit);
             p.kv_per_split = (n_kv + want - 1) / want;

@@ -138,6 +138,20 @@ def test_static_scratch_allocates_nothing(ncz, fake):
     assert len(fake.launches) == 4 and fake.created["alloc"] == 0
 
 
+def test_static_scratch_unsplit_request_runs_when_one_split_does_not_fit(ncz, fake):
+    """bh=8, S=8192, d=64: one split's partials (8*8192*66 floats) exceed the
+    scratch.  A request that makes no split (1, or the automatic count, which
+    the plan leaves at 1 for a grid this full) writes no partials and runs;
+    an explicit 2 still has to fit and is refused."""
+    lib = ncz.flash.lib()
+    x = desc(ncz, 0, bh=8, seq=8192)
+    assert lib.ncz_flash_fwd_static(ctypes.byref(x), 1) == 0
+    assert lib.ncz_flash_fwd_static(ctypes.byref(x), 0) == 0
+    assert labels(ncz, fake.launches) == ["flash_fwd<64,tma,f16>"] * 2
+    assert status(ncz, lib.ncz_flash_fwd_static(ctypes.byref(x), 2)) == "OutOfMemory"
+    assert len(fake.launches) == 2 and fake.created["alloc"] == 0 and fake.created["pool"] == 0
+
+
 def test_device_selection_failures(ncz, fake):
     fake.fail("set_device", device=6, error=F.INVALID_DEVICE)
     assert status(ncz, fwd(ncz, desc(ncz, 6))) == "InvalidDevice"

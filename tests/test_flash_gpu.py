@@ -367,7 +367,7 @@ def test_static_scratch_entry_matches_pool_path(ncz, oracle_mod):
     C.check(a.cpu().numpy(), C.reference(p, oracle_mod), C.active_index(p), "static scratch bh=1 S=4096")
 
 
-@pytest.mark.parametrize("bh,splits,fits", [(2, 0, 3), (2, 3, 3), (2, 4, 0), (4, 8, 0), (4, 0, 1)])
+@pytest.mark.parametrize("bh,splits,fits", [(2, 0, 3), (2, 3, 3), (2, 4, 0), (4, 8, 0), (4, 0, 1), (8, 1, 1)])
 def test_static_scratch_split_count_must_fit(ncz, oracle_mod, bh, splits, fits):
     """16 MiB of scratch holds 4 Mi floats: at S=8192, d=64 one split of bh slices
     needs bh*8192*66 floats.  The automatic count (0) runs what fits (bh=2: 3
