@@ -15,6 +15,12 @@ src/main.zig:1042); rel = |a - b| / max(|b|, 1e-3).
     python not-cute-zig_b200/compare.py --shape 8,1024,64,1 --gpus 2 --jsonl out.jsonl
     python not-cute-zig_b200/compare.py --shape 4,1000,32,1 --row-stride 40 --in-dtype bf16 --o-dtype f16 --seed 7
     python not-cute-zig_b200/compare.py --mma        # GEMM + epilogue (compareMma, src/main.zig:953-975)
+    python not-cute-zig_b200/compare.py --join ours.jsonl sdpa.jsonl cuda.jsonl   # joined table
+
+--join reads JSONL records of several harnesses (this one, the reference's
+tools/cuda_baselines.cu and tools/pytorch_baselines.py) and prints, per
+(kernel, shape), this library's time against every other implementation's,
+as the reference's modal_run.py:34-69 joins them.
 """
 from __future__ import annotations
 
@@ -244,6 +250,48 @@ def compare_mma(ncz, batches: int, k_iters: int, epilogue: int) -> dict:
 
 
 MMA_SHAPES = [(1, 1, 0), (1 << 21, 1, 1), (1 << 20, 4, 2), (1 << 18, 16, 3)]
+OURS = "not_cute_zig_b200"
+
+
+def read_records(paths: List[str]) -> List[dict]:
+    """JSON records, one per line, of every file (other lines are skipped)."""
+    out = []
+    for path in paths:
+        with open(path) as f:
+            for line in f:
+                line = line.strip()
+                if line.startswith("{"):
+                    try:
+                        out.append(json.loads(line))
+                    except json.JSONDecodeError:
+                        continue
+    return out
+
+
+def join_table(records: List[dict]) -> List[str]:
+    """Markdown rows: per (kernel, shape) with a record of this library, one row
+    per other implementation: both mean times, their ratio (other / ours) and
+    whether both records are correct (the reference's join, modal_run.py:34-69)."""
+    by_case: dict = {}
+    for r in records:
+        if r.get("gpus", 1) not in (1, None):
+            continue
+        by_case.setdefault((r.get("kernel"), r.get("shape")), {})[r.get("implementation")] = r
+    rows = ["| kernel | shape | baseline | ours ms | baseline ms | baseline / ours | both correct |",
+            "|---|---|---|---|---|---|---|"]
+    for (kernel, shape), impls in sorted(by_case.items(), key=lambda kv: (str(kv[0][0]), str(kv[0][1]))):
+        ours = impls.get(OURS)
+        if ours is None:
+            continue
+        for name in sorted(impls):
+            if name == OURS:
+                continue
+            other = impls[name]
+            ratio = other["mean_ms"] / ours["mean_ms"] if ours["mean_ms"] else 0.0
+            ok = "yes" if ours.get("correct") and other.get("correct") else "no"
+            rows.append(f"| {kernel} | {shape} | {name} | {ours['mean_ms']:.4f} | {other['mean_ms']:.4f} | "
+                        f"{ratio:.2f}x | {ok} |")
+    return rows
 
 
 def main(argv=None) -> int:
@@ -264,7 +312,12 @@ def main(argv=None) -> int:
                     help="the GEMM + epilogue records instead: compareMma's 16x8x16 and batched throughput shapes")
     ap.add_argument("--mma-shape", action="append", default=[],
                     help="batches,k_iters,epilogue (repeatable; implies --mma)")
+    ap.add_argument("--join", nargs="+", default=None, metavar="JSONL",
+                    help="print the joined table of these record files (no GPU work)")
     args = ap.parse_args(argv)
+    if args.join:
+        print("\n".join(join_table(read_records(args.join))))
+        return 0
     ncz = importlib.import_module("not-cute-zig_b200")
     bench = importlib.import_module("not-cute-zig_b200.benchmark")
     if args.mma or args.mma_shape:

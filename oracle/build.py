@@ -6,6 +6,10 @@
 - _ref/libncz_ref.so and _ref/cuda_baselines: the reference's own
   tools/cuda_baselines.cu compiled from where it lies in the reference tree
   (only when that tree is present); they travel to GPU boxes as built files.
+- _ref/pytorch_baselines.py: the reference's SDPA comparator
+  (tools/pytorch_baselines.py) staged unmodified beside them, so a GPU box can
+  run it (`python oracle/_ref/pytorch_baselines.py`); its JSONL joins with
+  compare.py's records (`compare.py --join`).
 """
 from __future__ import annotations
 
@@ -18,6 +22,7 @@ ORACLE_SO = os.path.join(HERE, "liboracle.so")
 REF_DIR = os.path.join(HERE, "_ref")
 REF_SO = os.path.join(REF_DIR, "libncz_ref.so")
 REF_BIN = os.path.join(REF_DIR, "cuda_baselines")
+REF_SDPA = os.path.join(REF_DIR, "pytorch_baselines.py")
 # The reference checkout sits beside this repository ("reference/" next to the
 # repository root) unless NCZ_REFERENCE_ROOT names another place.
 REFERENCE_ROOT = os.environ.get("NCZ_REFERENCE_ROOT",
@@ -61,6 +66,9 @@ def build_reference(force: bool = False) -> bool:
               "-shared", "-Dmain=ncz_reference_baselines_main", "-I", tools, harness, "-lcublas", "-o", REF_SO])
     if force or _stale(REF_BIN, [src]):
         _run([NVCC, "-O3", "-std=c++17", "-arch=sm_100a", src, "-lcublas", "-o", REF_BIN])
+    sdpa = os.path.join(tools, "pytorch_baselines.py")
+    if os.path.exists(sdpa) and (force or _stale(REF_SDPA, [sdpa])):
+        shutil.copyfile(sdpa, REF_SDPA)
     return True
 
 

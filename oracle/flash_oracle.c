@@ -66,10 +66,16 @@ static inline f16bits f2h(float f) {
 }
 
 /* Restates computeFlashReferenceOne (src/main.zig:1271-1307) for one
- * batch x head slice; `scores` is caller-provided scratch of seq_len floats. */
+ * batch x head slice; `scores` is caller-provided scratch of seq_len floats.
+ * When `mag` is given it also receives, per output element, sum_k w_k |v_k|
+ * with the same normalised weights w_k: the magnitude that bounds the effect
+ * of rounding the weights (the reference GPU kernels round P to f16,
+ * src/flash_h64_bn32.zig:185) on that output, |sum_k d_k w_k v_k| <= u * mag
+ * when every |d_k| <= u.  It is test bookkeeping, not part of the restated
+ * algorithm. */
 static void flash_one_row(size_t seq_len, size_t head_dim, size_t row, const f16bits *q,
                           size_t q_row, const f16bits *k, size_t k_row, const f16bits *v,
-                          size_t v_row, float *o, size_t o_row, float scale, uint32_t causal,
+                          size_t v_row, float *o, float *mag, size_t o_row, float scale, uint32_t causal,
                           float *scores, int bf16) {
     float (*const in)(f16bits) = bf16 ? b2f : h2f; /* Q/K/V element type */
     float row_max = -INFINITY;
@@ -99,6 +105,14 @@ static void flash_one_row(size_t seq_len, size_t head_dim, size_t row, const f16
         }
         o[row * o_row + col] = acc;
     }
+    if (mag != NULL) {
+        for (size_t col = 0; col < head_dim; ++col) {
+            double acc = 0.0;
+            for (size_t key = 0; key < seq_len; ++key)
+                acc += (double)(scores[key] / row_sum) * fabs((double)in(v[key * v_row + col]));
+            mag[row * o_row + col] = (float)acc;
+        }
+    }
 }
 
 /*
@@ -112,7 +126,7 @@ static void flash_one_row(size_t seq_len, size_t head_dim, size_t row, const f16
 static void oracle_flash(size_t batch_heads, size_t seq_len, size_t head_dim, const f16bits *q,
                          size_t q_stride, size_t q_row, const f16bits *k, size_t k_stride,
                          size_t k_row, const f16bits *v, size_t v_stride, size_t v_row, float *o,
-                         size_t o_stride, size_t o_row, float scale, uint32_t causal,
+                         float *mag, size_t o_stride, size_t o_row, float scale, uint32_t causal,
                          size_t row_begin, size_t row_end, int nthreads, int bf16) {
     if (row_end > seq_len) row_end = seq_len;
     if (row_begin >= row_end || batch_heads == 0) return;
@@ -132,7 +146,8 @@ static void oracle_flash(size_t batch_heads, size_t seq_len, size_t head_dim, co
             const size_t row = row_begin + (size_t)i % rows;
             flash_one_row(seq_len, head_dim, row, q + slice * q_stride, q_row,
                           k + slice * k_stride, k_row, v + slice * v_stride, v_row,
-                          o + slice * o_stride, o_row, scale, causal, scores, bf16);
+                          o + slice * o_stride, mag != NULL ? mag + slice * o_stride : NULL, o_row, scale,
+                          causal, scores, bf16);
         }
         free(scores);
     }
@@ -144,7 +159,18 @@ void ncz_oracle_flash(size_t batch_heads, size_t seq_len, size_t head_dim, const
                       size_t o_stride, size_t o_row, float scale, uint32_t causal,
                       size_t row_begin, size_t row_end, int nthreads) {
     oracle_flash(batch_heads, seq_len, head_dim, q, q_stride, q_row, k, k_stride, k_row, v, v_stride,
-                 v_row, o, o_stride, o_row, scale, causal, row_begin, row_end, nthreads, 0);
+                 v_row, o, NULL, o_stride, o_row, scale, causal, row_begin, row_end, nthreads, 0);
+}
+
+/* ncz_oracle_flash plus, in `mag` (laid out like o), the per-element magnitude
+ * sum_k w_k |v_k| (see flash_one_row); bf16 != 0 reads bf16 Q/K/V. */
+void ncz_oracle_flash_mag(size_t batch_heads, size_t seq_len, size_t head_dim, const f16bits *q,
+                          size_t q_stride, size_t q_row, const f16bits *k, size_t k_stride,
+                          size_t k_row, const f16bits *v, size_t v_stride, size_t v_row, float *o,
+                          float *mag, size_t o_stride, size_t o_row, float scale, uint32_t causal,
+                          size_t row_begin, size_t row_end, int nthreads, int bf16) {
+    oracle_flash(batch_heads, seq_len, head_dim, q, q_stride, q_row, k, k_stride, k_row, v, v_stride,
+                 v_row, o, mag, o_stride, o_row, scale, causal, row_begin, row_end, nthreads, bf16 != 0);
 }
 
 /* The same maths on bf16 Q/K/V (the reference has f16 only; this extends the
@@ -155,7 +181,7 @@ void ncz_oracle_flash_bf16(size_t batch_heads, size_t seq_len, size_t head_dim, 
                            size_t o_stride, size_t o_row, float scale, uint32_t causal,
                            size_t row_begin, size_t row_end, int nthreads) {
     oracle_flash(batch_heads, seq_len, head_dim, q, q_stride, q_row, k, k_stride, k_row, v, v_stride,
-                 v_row, o, o_stride, o_row, scale, causal, row_begin, row_end, nthreads, 1);
+                 v_row, o, NULL, o_stride, o_row, scale, causal, row_begin, row_end, nthreads, 1);
 }
 
 /* fillFlashInput (src/main.zig:1207-1211):
@@ -179,31 +205,58 @@ static inline double uniform01(uint64_t *state) {
     return ((double)(splitmix64(state) >> 11) + 0.5) * (1.0 / 9007199254740992.0);
 }
 
-/* f16(mean + std * N(0,1)); Box-Muller on pairs from splitmix64(seed). */
-static void fill_normal_as(f16bits *data, size_t n, uint64_t seed, float mean, float stddev,
+/* The generator is counter based: after c draws from seed the state is
+ * seed + c * 0x9E3779B97F4A7C15 (mod 2^64), so any stretch of the stream can
+ * be produced on its own, and in parallel, with the same bits. */
+#define NCZ_GOLDEN_GAMMA 0x9E3779B97F4A7C15ull
+
+/* Elements first .. first+n-1 of the stream f16(mean + std * N(0,1)): element
+ * 2p and 2p+1 are the cos and sin halves of the Box-Muller pair made from
+ * draws 2p and 2p+1 of splitmix64(seed). */
+static void fill_normal_as(f16bits *data, size_t n, uint64_t seed, size_t first, float mean, float stddev,
                            f16bits (*enc)(float)) {
-    uint64_t state = seed;
     const double two_pi = 6.283185307179586476925286766559;
-    for (size_t i = 0; i < n; i += 2) {
+    const size_t end = first + n;
+    const size_t p0 = first / 2, p1 = (end + 1) / 2;  /* pairs touched */
+    const ptrdiff_t np = (ptrdiff_t)(p1 - p0);
+#pragma omp parallel for schedule(static) if (np > 65536)
+    for (ptrdiff_t j = 0; j < np; ++j) {
+        const size_t pair = p0 + (size_t)j;
+        uint64_t state = seed + (uint64_t)(2 * pair) * NCZ_GOLDEN_GAMMA;
         const double u1 = uniform01(&state), u2 = uniform01(&state);
         const double r = sqrt(-2.0 * log(u1));
-        data[i] = enc((float)(mean + stddev * r * cos(two_pi * u2)));
-        if (i + 1 < n) data[i + 1] = enc((float)(mean + stddev * r * sin(two_pi * u2)));
+        const size_t e0 = 2 * pair, e1 = e0 + 1;
+        if (e0 >= first && e0 < end) data[e0 - first] = enc((float)(mean + stddev * r * cos(two_pi * u2)));
+        if (e1 >= first && e1 < end) data[e1 - first] = enc((float)(mean + stddev * r * sin(two_pi * u2)));
     }
 }
 
 void ncz_oracle_fill_normal(f16bits *data, size_t n, uint64_t seed, float mean, float stddev) {
-    fill_normal_as(data, n, seed, mean, stddev, f2h);
+    fill_normal_as(data, n, seed, 0, mean, stddev, f2h);
+}
+
+/* ncz_oracle_fill_normal's stream from element `first` on. */
+void ncz_oracle_fill_normal_range(f16bits *data, size_t n, uint64_t seed, size_t first, float mean, float stddev) {
+    fill_normal_as(data, n, seed, first, mean, stddev, f2h);
 }
 
 /* bf16 (round to nearest even) from the same splitmix64 + Box-Muller stream. */
 void ncz_oracle_fill_normal_bf16(f16bits *data, size_t n, uint64_t seed, float mean, float stddev) {
-    fill_normal_as(data, n, seed, mean, stddev, f2b);
+    fill_normal_as(data, n, seed, 0, mean, stddev, f2b);
+}
+
+/* Elements first .. first+n-1 of f16(U(lo, hi)): element i from draw i. */
+void ncz_oracle_fill_uniform_range(f16bits *data, size_t n, uint64_t seed, size_t first, float lo, float hi) {
+    const ptrdiff_t nn = (ptrdiff_t)n;
+#pragma omp parallel for schedule(static) if (nn > 65536)
+    for (ptrdiff_t j = 0; j < nn; ++j) {
+        uint64_t state = seed + (uint64_t)(first + (size_t)j) * NCZ_GOLDEN_GAMMA;
+        data[j] = f2h((float)(lo + (hi - lo) * uniform01(&state)));
+    }
 }
 
 void ncz_oracle_fill_uniform(f16bits *data, size_t n, uint64_t seed, float lo, float hi) {
-    uint64_t state = seed;
-    for (size_t i = 0; i < n; ++i) data[i] = f2h((float)(lo + (hi - lo) * uniform01(&state)));
+    ncz_oracle_fill_uniform_range(data, n, seed, 0, lo, hi);
 }
 
 /* Sets every element of a strided [batch_heads, seq_len, row] view whose

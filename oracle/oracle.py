@@ -31,6 +31,9 @@ def lib() -> ctypes.CDLL:
                                        ctypes.c_float, ctypes.c_uint32, sz, sz, ctypes.c_int]
         h.ncz_oracle_flash_bf16.restype = None
         h.ncz_oracle_flash_bf16.argtypes = h.ncz_oracle_flash.argtypes
+        h.ncz_oracle_flash_mag.restype = None
+        h.ncz_oracle_flash_mag.argtypes = [sz, sz, sz, vp, sz, sz, vp, sz, sz, vp, sz, sz, vp, vp, sz, sz,
+                                           ctypes.c_float, ctypes.c_uint32, sz, sz, ctypes.c_int, ctypes.c_int]
         h.ncz_oracle_fill_normal_bf16.restype = None
         h.ncz_oracle_fill_normal_bf16.argtypes = [vp, sz, ctypes.c_uint64, ctypes.c_float, ctypes.c_float]
         h.ncz_oracle_fill_pattern.restype = None
@@ -39,6 +42,10 @@ def lib() -> ctypes.CDLL:
         h.ncz_oracle_fill_normal.argtypes = [vp, sz, ctypes.c_uint64, ctypes.c_float, ctypes.c_float]
         h.ncz_oracle_fill_uniform.restype = None
         h.ncz_oracle_fill_uniform.argtypes = [vp, sz, ctypes.c_uint64, ctypes.c_float, ctypes.c_float]
+        h.ncz_oracle_fill_normal_range.restype = None
+        h.ncz_oracle_fill_normal_range.argtypes = [vp, sz, ctypes.c_uint64, sz, ctypes.c_float, ctypes.c_float]
+        h.ncz_oracle_fill_uniform_range.restype = None
+        h.ncz_oracle_fill_uniform_range.argtypes = [vp, sz, ctypes.c_uint64, sz, ctypes.c_float, ctypes.c_float]
         h.ncz_oracle_fill_row_padding.restype = None
         h.ncz_oracle_fill_row_padding.argtypes = [vp, sz, sz, sz, sz, sz, ctypes.c_uint16]
         h.ncz_oracle_max_threads.restype = ctypes.c_int
@@ -61,17 +68,18 @@ def fill_pattern(n: int, mul: int, add: int, scale: float, modulus: int = 17) ->
     return out
 
 
-def fill_normal(n: int, seed: int, mean: float = 0.0, std: float = 1.0) -> np.ndarray:
-    """f16(mean + std * N(0,1)) from splitmix64(seed) + Box-Muller."""
+def fill_normal(n: int, seed: int, mean: float = 0.0, std: float = 1.0, first: int = 0) -> np.ndarray:
+    """f16(mean + std * N(0,1)) from splitmix64(seed) + Box-Muller: elements
+    first .. first+n-1 of the stream (the same bits as a longer fill's slice)."""
     out = np.empty(n, dtype=np.float16)
-    lib().ncz_oracle_fill_normal(_ptr(out), n, seed, mean, std)
+    lib().ncz_oracle_fill_normal_range(_ptr(out), n, seed, first, mean, std)
     return out
 
 
-def fill_uniform(n: int, seed: int, lo: float = -1.0, hi: float = 1.0) -> np.ndarray:
-    """f16(U(lo, hi)) from splitmix64(seed)."""
+def fill_uniform(n: int, seed: int, lo: float = -1.0, hi: float = 1.0, first: int = 0) -> np.ndarray:
+    """f16(U(lo, hi)) from splitmix64(seed): elements first .. first+n-1 of the stream."""
     out = np.empty(n, dtype=np.float16)
-    lib().ncz_oracle_fill_uniform(_ptr(out), n, seed, lo, hi)
+    lib().ncz_oracle_fill_uniform_range(_ptr(out), n, seed, first, lo, hi)
     return out
 
 
@@ -86,12 +94,16 @@ def fill_row_padding(a: np.ndarray, batch_heads: int, seq_len: int, head_dim: in
 def flash_reference(q: np.ndarray, k: np.ndarray, v: np.ndarray, *, batch_heads: int, seq_len: int,
                     head_dim: int, q_stride: int, k_stride: int, v_stride: int, o_stride: int,
                     scale: float, causal: bool, row_strides=None, out: np.ndarray | None = None,
-                    rows: tuple[int, int] | None = None, threads: int = 0) -> np.ndarray:
+                    rows: tuple[int, int] | None = None, threads: int = 0,
+                    mag: np.ndarray | None = None) -> np.ndarray:
     """The reference CPU attention over all slices (computeFlashReferenceSlices,
     src/main.zig:1242-1269), with optional per-row strides (default head_dim).
 
     Returns a float32 array of batch_heads * o_stride elements (unwritten
-    elements are 0, as the reference's `expected` buffer is zero-filled)."""
+    elements are 0, as the reference's `expected` buffer is zero-filled).
+    `mag` (float32, laid out like out) receives sum_k w_k |v_k| per output
+    element: the scale of the error that rounding the weights P (relative
+    error <= u each) can cause, at most u * mag."""
     qr, kr, vr, orow = row_strides if row_strides is not None else (head_dim,) * 4
     bf16 = q.dtype == np.uint16  # bf16 bit patterns (numpy has no bf16 type)
     for a in (q, k, v):
@@ -99,6 +111,12 @@ def flash_reference(q: np.ndarray, k: np.ndarray, v: np.ndarray, *, batch_heads:
     if out is None:
         out = np.zeros(batch_heads * o_stride, dtype=np.float32)
     r0, r1 = rows if rows is not None else (0, seq_len)
+    if mag is not None:
+        assert mag.dtype == np.float32 and mag.size >= out.size
+        lib().ncz_oracle_flash_mag(batch_heads, seq_len, head_dim, _ptr(q), q_stride, qr, _ptr(k), k_stride, kr,
+                                   _ptr(v), v_stride, vr, _ptr(out), _ptr(mag), o_stride, orow, float(scale),
+                                   int(bool(causal)), r0, r1, threads, int(bf16))
+        return out
     fn = lib().ncz_oracle_flash_bf16 if bf16 else lib().ncz_oracle_flash
     fn(batch_heads, seq_len, head_dim, _ptr(q), q_stride, qr, _ptr(k), k_stride, kr,
        _ptr(v), v_stride, vr, _ptr(out), o_stride, orow, float(scale), int(bool(causal)), r0, r1, threads)

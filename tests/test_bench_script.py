@@ -59,3 +59,30 @@ def test_reference_arm_json_line():
     assert line["e2e"] == {"value": line["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                            "d2h_bytes_per_step": 0}
     assert line["config"]["head_dim"] == 32 and "row stride 40" in line["config"]["workload"]
+
+
+def test_parity_check_gate(bench, oracle_mod):
+    """bench.py's per-rank parity record: the oracle's own output passes; an
+    error just inside both bounds (ATOL, and 1e-2 * max(|O|, 1e-3) + u * mag)
+    passes, twice that fails; the slice checked is the middle one of the
+    rank's range."""
+    name = "c2"
+    bh, s, d = 3, 300, 64
+    _, _, _, causal, std, k_mul, seed, _, _ = bench.WORKLOADS[name]
+    hq, hk, hv = bench.make_inputs(oracle_mod, bh, s, d, std, k_mul, seed)
+    want = np.zeros(bh * s * d, dtype=np.float32)
+    mag = np.zeros_like(want)
+    oracle_mod.flash_reference(hq, hk, hv, batch_heads=bh, seq_len=s, head_dim=d, q_stride=s * d, k_stride=s * d,
+                               v_stride=s * d, o_stride=s * d, scale=d ** -0.5, causal=causal, out=want, mag=mag)
+    old = bench.WORKLOADS[name]
+    bench.WORKLOADS[name] = (bh, s, d) + old[3:]
+    try:
+        rec = bench.parity_check(oracle_mod, name, hq, hk, hv, want.copy(), 5, 5 + bh)
+        assert rec["ok"] and rec["max_abs"] == 0.0 and rec["slice"] == 6 and rec["rows"] == [[0, 128], [172, 300]]
+        edge = 0.99 * np.minimum(bench.RTOL * np.maximum(np.abs(want), bench.REL_FLOOR) + bench.P_UNIT * mag,
+                                 bench.ATOL)
+        assert bench.parity_check(oracle_mod, name, hq, hk, hv, want + edge, 5, 5 + bh)["ok"]
+        bad = bench.parity_check(oracle_mod, name, hq, hk, hv, want + 2 * edge, 5, 5 + bh)
+        assert not bad["ok"] and bad["violations"] > 0 and bad["max_abs"] > bench.ATOL
+    finally:
+        bench.WORKLOADS[name] = old

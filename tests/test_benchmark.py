@@ -82,3 +82,26 @@ def test_host_reference_time(compare):
     q, k, v = (torch.randn(2 * 64 * 32).half() for _ in range(3))
     ms = compare.host_reference_ms(q, k, v, 2, 64, 32, 32 ** -0.5, True)
     assert 0.0 < ms < 60_000.0
+
+
+def test_join_table_pairs_our_records_with_each_baseline(compare, tmp_path):
+    """--join: one row per (kernel, shape, other implementation), ratio other / ours;
+    multi-GPU records and shapes without a record of ours are left out."""
+    shape = "batch_heads=8,seq=1024,head=64,causal=true"
+    recs = [
+        {"kernel": "flash_attention", "implementation": compare.OURS, "shape": shape, "mean_ms": 0.02, "correct": True},
+        {"kernel": "flash_attention", "implementation": compare.OURS, "shape": shape, "mean_ms": 0.5, "correct": True,
+         "gpus": 2},
+        {"kernel": "flash_attention", "implementation": "torch_sdpa_flash", "shape": shape, "mean_ms": 0.05,
+         "correct": True},
+        {"kernel": "flash_attention", "implementation": "cuda_wmma", "shape": shape, "mean_ms": 0.4, "correct": False},
+        {"kernel": "flash_attention", "implementation": "torch_sdpa_math", "shape": "other", "mean_ms": 1.0,
+         "correct": True},
+    ]
+    a, b = tmp_path / "a.jsonl", tmp_path / "b.jsonl"
+    a.write_text("\n".join(json.dumps(r) for r in recs[:2]) + "\nnot json\n")
+    b.write_text("\n".join(json.dumps(r) for r in recs[2:]) + "\n")
+    rows = compare.join_table(compare.read_records([str(a), str(b)]))
+    assert len(rows) == 4
+    assert "| cuda_wmma | 0.0200 | 0.4000 | 20.00x | no |" in rows[2]
+    assert "| torch_sdpa_flash | 0.0200 | 0.0500 | 2.50x | yes |" in rows[3]

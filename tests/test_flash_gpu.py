@@ -78,11 +78,8 @@ def test_config2_profile_f16_out(ncz, oracle_mod):
     """bh=8, S=1024, d=64, causal, N(0, 0.5^2) seed 1, f16 O."""
     p = C.normal_problem(8, 1024, 64, True, 1, oracle_mod, std=0.5)
     got = run(ncz, p, o_dtype="float16")
-    want = C.reference(p, oracle_mod)
-    idx = C.active_index(p)
-    err = np.abs(got[idx].astype(np.float64) - want[idx])
     # f16 output adds at most half an f16 ulp of |O| on top of the f32 tolerance.
-    assert np.all(err <= C.ATOL + np.abs(want[idx]) * 2.0 ** -11), err.max()
+    C.check(got, C.reference(p, oracle_mod), C.active_index(p), "config2 f16 O", o_unit=2.0 ** -11)
 
 
 def test_config3_padded_rows_nan_pad(ncz, oracle_mod):
@@ -253,7 +250,8 @@ def test_host_pipeline_matches_device_launch(ncz, oracle_mod, chunk, o_dtype):
     idx = C.active_index(p)
     ti = torch.from_numpy(idx)
     assert torch.equal(got[ti], want[ti])
-    C.check(got.float().numpy(), C.reference(p, oracle_mod), idx, f"host pipeline chunk={chunk} {o_dtype}")
+    C.check(got.float().numpy(), C.reference(p, oracle_mod), idx, f"host pipeline chunk={chunk} {o_dtype}",
+            o_unit=2.0 ** -11 if o_dtype == "float16" else 0.0)
 
 
 SPLIT_CASES = [(4, 1024, 64, True), (3, 1000, 64, False), (2, 777, 32, True), (5, 1300, 16, True),
@@ -285,11 +283,11 @@ def test_config2_split_and_unsplit_match(ncz, oracle_mod):
     before = ncz.flash.launch_count()
     auto = run(ncz, p, o_dtype="float16", splits=0)
     assert ncz.flash.launch_count() - before == 1
-    C.check(auto, want, idx, "config 2 auto (f16 O)")
+    C.check(auto, want, idx, "config 2 auto (f16 O)", o_unit=2.0 ** -11)
     before = ncz.flash.launch_count()
     split = run(ncz, p, o_dtype="float16", splits=4)
     assert ncz.flash.launch_count() - before == 2  # forward + combine
-    C.check(split, want, idx, "config 2 split 4 (f16 O)")
+    C.check(split, want, idx, "config 2 split 4 (f16 O)", o_unit=2.0 ** -11)
 
 
 def test_long_sequence_few_slices_splits_automatically(ncz, oracle_mod):
@@ -548,7 +546,8 @@ def test_bf16_inputs_match_oracle(ncz, oracle_mod, case, producer):
     p = C.normal_problem_bf16(bh, s, d, causal, 23, oracle_mod, std=0.8)
     got = _run_bf16(ncz, p, producer=producer)
     idx = C.active_index(p)
-    C.check(got, C.reference(p, oracle_mod), idx, f"bf16 {case} {producer}", atol=C.ATOL_BF16)
+    C.check(got, C.reference(p, oracle_mod), idx, f"bf16 {case} {producer}", atol=C.ATOL_BF16,
+            p_unit=C.P_UNIT_BF16)
     assert untouched(got, p, idx)
     if producer == "lsu":
         assert np.array_equal(got, _run_bf16(ncz, p, producer="tma"))
@@ -558,20 +557,23 @@ def test_bf16_inputs_match_oracle(ncz, oracle_mod, case, producer):
 def test_bf16_inputs_16bit_outputs(ncz, oracle_mod, o_dtype):
     p = C.normal_problem_bf16(3, 700, 64, True, 29, oracle_mod, std=0.7)
     got = _run_bf16(ncz, p, o_dtype=o_dtype)
-    C.check(got, C.reference(p, oracle_mod), C.active_index(p), f"bf16 in, {o_dtype} out", atol=C.ATOL_BF16)
+    C.check(got, C.reference(p, oracle_mod), C.active_index(p), f"bf16 in, {o_dtype} out", atol=C.ATOL_BF16,
+            p_unit=C.P_UNIT_BF16)
 
 
 def test_bf16_split_kv(ncz, oracle_mod):
     p = C.normal_problem_bf16(1, 4096, 64, True, 31, oracle_mod, std=0.7)
     got = _run_bf16(ncz, p, splits=4)
-    C.check(got, C.reference(p, oracle_mod), C.active_index(p), "bf16 split-KV", atol=C.ATOL_BF16)
+    C.check(got, C.reference(p, oracle_mod), C.active_index(p), "bf16 split-KV", atol=C.ATOL_BF16,
+            p_unit=C.P_UNIT_BF16)
 
 
 def test_bf16_output_from_f16_inputs(ncz, oracle_mod):
     """bf16 O from f16 inputs (O type is independent of the input type)."""
     p = C.normal_problem(2, 300, 32, False, 37, oracle_mod, std=0.7)
     got = run(ncz, p, o_dtype="bfloat16")
-    C.check(got, C.reference(p, oracle_mod), C.active_index(p), "f16 in, bf16 out", atol=C.ATOL_BF16)
+    C.check(got, C.reference(p, oracle_mod), C.active_index(p), "f16 in, bf16 out", atol=C.ATOL_BF16,
+            o_unit=2.0 ** -8)
 
 
 def test_many_items_per_cta_with_empty_q_tiles(ncz, oracle_mod):

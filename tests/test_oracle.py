@@ -132,3 +132,16 @@ def test_bf16_generator_rounds_to_nearest_even(oracle_mod):
     assert np.abs(b - h.astype(np.float32)).max() <= 2.0 ** -7 * np.abs(b).max()
     # bf16 values have no bits below the top 16
     assert np.all((b.view(np.uint32) & 0xFFFF) == 0)
+
+
+@pytest.mark.parametrize("first,n", [(0, 5), (1, 10), (3, 9998), (10000, 10001), (20000, 1)])
+def test_fill_ranges_are_slices_of_the_whole_stream(oracle_mod, first, n):
+    """The generators are counter based: a fill from element `first` equals the
+    same elements of a fill from 0 (odd starts take the sin half of a pair),
+    so each rank can generate only its own slices of a workload."""
+    full = oracle_mod.fill_normal(20001, 9, 0.0, 1.0)
+    part = oracle_mod.fill_normal(n, 9, 0.0, 1.0, first=first)
+    assert np.array_equal(full[first:first + n].view(np.uint16), part.view(np.uint16))
+    fu = oracle_mod.fill_uniform(20001, 9, -1.0, 1.0)
+    pu = oracle_mod.fill_uniform(n, 9, -1.0, 1.0, first=first)
+    assert np.array_equal(fu[first:first + n].view(np.uint16), pu.view(np.uint16))
