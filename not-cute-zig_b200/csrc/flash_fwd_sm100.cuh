@@ -831,37 +831,25 @@ __device__ __forceinline__ void softmax_role(const FlashParams &p, uint8_t *smem
         stash[1] = it;
         float m = -INFINITY;  // exponent base: scaled row max, log2 domain (stale by < 8)
         float l = 0.0f;       // running sum of 2^(x - m)
-        // Per K tile j: compute(j) waits for the tile's scores, releases S,
-        // takes the row max and exponentiates into P registers; store_p(j)
-        // waits for PV(j-1), rebases O if the max moved, and stores P(j) to
-        // TMEM; finish_p() signals P(j) to the MMA warp.  The loop runs them
-        // as store_p(j-1), load of S(j), finish_p(), compute(j): the scores'
-        // TMEM load is in flight during the previous tile's P store and
-        // hand-off instead of standing between two tiles' exponentials, and
-        // only P (64 registers) crosses from one iteration to the next.  The
-        // first tile has no PV to wait for and no O to rebase, and only the
-        // last can hold masked keys (K tile index diag, or a ragged end); both
-        // are peeled (`first` and `final` are compile-time flags), so the loop
-        // over the other tiles carries neither branch (peeling measured about
-        // 6 % per tile at d=64 with the tile loop nested in the item loop).
-        uint32_t sr[kBlockN];     // scores of the tile being loaded (asynchronous TMEM load)
-        uint32_t pk[kBlockN / 2];  // P of the last exponentiated tile (f16 / bf16 pairs)
-        float alpha = 1.0f;        // rebase factor of that tile
-        bool need = false;         // some row of the warp rebases at that tile
-        auto load_s = [&](int j) -> bool {
+        // One K tile.  The first of an item has no PV to wait for and no O to
+        // rescale, and only the last can hold masked keys (K tile index diag,
+        // or a ragged end); both are issued apart (`first` and `final` are
+        // compile-time flags), so the loop over the other tiles carries neither
+        // branch.  With the tile loop nested in the item loop, peeling the first
+        // tile is worth about 6% per tile (measured at d=64).
+        auto tile = [&](int j, auto first, auto final) -> bool {
             if (!warp_wait(b.s_full(w), (ph + j) & 1, abort_flag, kSiteSFull)) return false;
             tc_fence_after();
-            tmem_ld_x128_async(tS, sr);
-            return true;
-        };
-        auto compute = [&](int j, auto final) {
-            tmem_wait_ld_x128(sr);
+            float x[kBlockN];
+            {
+                uint32_t sr[kBlockN];
+                tmem_ld_x128_wait(tS, sr);
+#pragma unroll
+                for (int c = 0; c < kBlockN; ++c) x[c] = __uint_as_float(sr[c]);
+            }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(b.s_free(w));  // S may be overwritten by the next QK^T
-            float x[kBlockN];
-#pragma unroll
-            for (int c = 0; c < kBlockN; ++c) x[c] = __uint_as_float(sr[c]);
             bool half = false;
             float mx;
             if constexpr (decltype(final)::value) {
@@ -885,23 +873,21 @@ __device__ __forceinline__ void softmax_role(const FlashParams &p, uint8_t *smem
                 mx = row_max(x);
             }
             const float m_new = fmaxf(m, mx * kmul);
-            const bool rebase = m_new > m + kRescaleThreshold;
-            float m_use = rebase ? m_new : m;
+            const bool need = m_new > m + kRescaleThreshold;
+            float m_use = need ? m_new : m;
             m_use = m_use == -INFINITY ? 0.0f : m_use;  // row with nothing visible yet
+            uint32_t pk[kBlockN / 2];
             const float tsum = half ? exp_row<kBf16, kBlockN / 2>(x, kmul, m_use, pk) : exp_row<kBf16>(x, kmul, m_use, pk);
-            alpha = ex2_approx(m - m_use);  // 1 when not rebasing, 0 on the first tile
+            const float alpha = ex2_approx(m - m_use);  // 1 when not rescaling, 0 on the first tile
             l = l * alpha + tsum;
             m = m_use;
-            need = __any_sync(0xffffffffu, rebase);
-        };
-        auto store_p = [&](int j, auto first) -> bool {
             if constexpr (!decltype(first)::value) {
                 // PV(j-1) reads P and accumulates into O: it must be done before P is
                 // overwritten and before O is rebased.  (At j = 0 the previous
                 // item's epilogue already waited for its last PV.)
                 if (!warp_wait(b.o_done(w), (ph + j - 1) & 1, abort_flag, kSiteODone)) return false;
                 tc_fence_after();
-                if (need) {
+                if (__any_sync(0xffffffffu, need)) {
                     // In chunks of at most 32 columns: fewer registers on this
                     // (rare) path, next to the 64 of P.
                     constexpr int kC = D < 32 ? D : 32;
@@ -916,48 +902,19 @@ __device__ __forceinline__ void softmax_role(const FlashParams &p, uint8_t *smem
                     }
                 }
             }
-            tmem_st_x64(tP, pk);  // the registers are read when the store issues
-            return true;
-        };
-        auto finish_p = [&]() {
+            tmem_st_x64(tP, pk);
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(b.p_full(w));
+            return true;
         };
-        ok = load_s(0);
-        if (!ok) break;
         if (n == 1) {
-            compute(0, std::true_type{});
-            ok = store_p(0, std::true_type{});
+            ok = tile(0, std::true_type{}, std::true_type{});
         } else {
-            compute(0, std::false_type{});
-            ok = store_p(0, std::true_type{}) && load_s(1);
-            if (ok) {
-                finish_p();
-                if (n == 2) {
-                    compute(1, std::true_type{});
-                } else {
-                    compute(1, std::false_type{});
-                    for (int j = 2; ok && j + 1 < n; ++j) {
-                        ok = store_p(j - 1, std::false_type{}) && load_s(j);
-                        if (!ok) break;
-                        finish_p();
-                        compute(j, std::false_type{});
-                    }
-                    if (ok) ok = store_p(n - 2, std::false_type{}) && load_s(n - 1);
-                    if (ok) {
-                        finish_p();
-                        compute(n - 1, std::true_type{});
-                    }
-                }
-                if (ok) ok = store_p(n - 1, std::false_type{});
-            }
-        }
-        if (ok) {
-            finish_p();
-        } else {
-            tmem_wait_st();  // a P store may still be in flight when a wait gave up
+            ok = tile(0, std::true_type{}, std::false_type{});
+            for (int j = 1; ok && j + 1 < n; ++j) ok = tile(j, std::false_type{}, std::false_type{});
+            if (ok) ok = tile(n - 1, std::false_type{}, std::true_type{});
         }
         if (!ok) break;
         // Epilogue: the item's last PV done, O read, O released to the next item's
