@@ -94,8 +94,12 @@ constexpr unsigned long long kWaitLimitCycles = 4000000000ull;
 #ifndef NCZ_EXP2_EMU_COUNT
 #define NCZ_EXP2_EMU_COUNT 0
 #endif
+#ifndef NCZ_EXP2_EMU_DEGREE
+#define NCZ_EXP2_EMU_DEGREE 4
+#endif
 constexpr int kExp2EmuPeriod = NCZ_EXP2_EMU_PERIOD;
 constexpr int kExp2EmuCount = NCZ_EXP2_EMU_COUNT;
+constexpr int kExp2EmuDegree = NCZ_EXP2_EMU_DEGREE;  // polynomial degree: 3 or 4
 
 // where a bounded wait gave up (bits 24..30 of the status word)
 enum WaitSite : uint32_t {
@@ -756,7 +760,11 @@ __device__ __forceinline__ float exp_row(float (&x)[kBlockN], float kmul, float 
         float e0, e1, p0, p1;
         unpack_f32x2(ffma2(pack_f32x2(x[2 * c], x[2 * c + 1]), kmul2, negm2), e0, e1);
         if (kExp2EmuPeriod > 0 && c % kExp2EmuPeriod >= kExp2EmuPeriod - kExp2EmuCount) {
-            exp2_poly_x2(e0, e1, p0, p1);  // FMA pipe
+            if constexpr (kExp2EmuDegree == 3) {
+                exp2_poly3_x2(e0, e1, p0, p1);  // FMA pipe
+            } else {
+                exp2_poly_x2(e0, e1, p0, p1);
+            }
         } else {
             p0 = ex2_approx(e0);  // MUFU
             p1 = ex2_approx(e1);

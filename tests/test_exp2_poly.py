@@ -63,3 +63,36 @@ def test_exact_at_integers_and_clamped_below():
     assert np.array_equal(got.astype(np.float64), np.exp2(e.astype(np.float64)))  # 2^0 == 1 held exactly
     low, _ = exp2_poly(np.float32([-np.inf, -300.0, -126.0]))
     assert np.all(low == np.float32(2.0 ** -125))
+
+
+def coefficients3():
+    text = open(HEADER).read()
+    body = text[text.index("void exp2_poly3_x2"):]
+    found = dict(re.findall(r"k(C[1-3]) = ([0-9.eE+-]+)f", body[:400]))
+    return [np.float32(found[f"C{i}"]) for i in range(1, 4)]
+
+
+def exp2_poly3(e):
+    c1, c2, c3 = coefficients3()
+    e = np.maximum(e.astype(np.float32), np.float32(-125.0))
+    r = np.float32(12582912.0)
+    t = (e + r).astype(np.float32)
+    n = (t - r).astype(np.float32)
+    f = fma32(n, np.float32(-1.0), e)
+    q = fma32(f, c3, c2)
+    q = fma32(q, f, c1)
+    q = fma32(q, f, np.float32(1.0))
+    return (q.astype(np.float64) * np.exp2(n.astype(np.float64))).astype(np.float32)
+
+
+def test_degree3_relative_error_within_a_fifth_of_the_f16_unit_roundoff():
+    """exp2_poly3_x2 (NCZ_EXP2_EMU_DEGREE=3): stated 1.02e-4, under 2^-11 / 4."""
+    e = np.concatenate([np.linspace(-125.0, 8.0, 2_000_001, dtype=np.float32),
+                        np.arange(-125, 9, dtype=np.float32) + np.float32(0.5)])
+    got = exp2_poly3(e)
+    want = np.exp2(e.astype(np.float64))
+    rel = np.abs(got.astype(np.float64) - want) / want
+    assert rel.max() <= 1.03e-4, rel.max()
+    assert rel.max() < 2.0 ** -11 / 4
+    ints = np.arange(-125, 9, dtype=np.float32)
+    assert np.array_equal(exp2_poly3(ints).astype(np.float64), np.exp2(ints.astype(np.float64)))
