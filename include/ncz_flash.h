@@ -253,6 +253,21 @@ int ncz_test_chunk_plan(size_t batch_heads, size_t chunk_slices, int taper, size
 int ncz_test_item_work(size_t batch_heads, size_t seq_len, uint32_t causal, int splits, int chunk_slices, int item,
                        int32_t *out);
 
+/* Test hook: the work item `item` of a launch of split-Q items (one 128-row
+ * Q tile per item, its K tiles alternating between the CTA's two pipelines;
+ * the library uses them when a launch without split-KV has too few items of
+ * two Q tiles to keep the SMs busy).  out[0..5] = slice, first Q row, K tiles
+ * of slot 0 (the even ones), of slot 1 (the odd ones), the item's K tiles,
+ * K tile stride (2).  Host only; NCZ_ERROR_INVALID_VALUE past the launch. */
+int ncz_test_qsplit_work(size_t batch_heads, size_t seq_len, uint32_t causal, int chunk_slices, int item,
+                         int32_t *out);
+
+/* Test hook: the split-Q choice of every following launch of this process:
+ * 0 automatic (the default), 1 whenever the launch has no split-KV, 2 never.
+ * Results agree either way within the parity bound; the hook lets tests run
+ * both item kinds on the same shape. */
+int ncz_test_set_qsplit(int mode);
+
 /* Bound of every in-kernel mbarrier wait on `device` (-1 = current), in SM
  * cycles; 0 restores the default (4e9, about 2 s).  A test shortens it so an
  * expired wait is seen quickly. */

@@ -52,8 +52,20 @@ constexpr int kVariants = 12;  // (D in 16/32/64) x (TMA, LSU) x (f16, bf16 inpu
 #ifndef NCZ_WALK_TILES
 #define NCZ_WALK_TILES (1 << 30)
 #endif
+// Split-Q items (one Q tile per item, its K tiles alternating between the two
+// pipelines) when the items of two Q tiles number fewer than this many per SM:
+// some SMs would idle and the longest item bounds the launch, so halving it
+// pays (config 2, 32 items: 22.7 -> 18.1 us).  With more items split-Q lost
+// 9-12 % (each K/V tile then feeds one pipeline instead of two, and there are
+// twice the items), so it stays off there.
+#ifndef NCZ_QSPLIT_ITEMS_PER_SM
+#define NCZ_QSPLIT_ITEMS_PER_SM 1
+#endif
 
 std::mutex g_mu;
+// Split-Q choice: 0 automatic, 1 whenever the launch has no split-KV, 2 never
+// (ncz_test_set_qsplit).
+std::atomic<int> g_qsplit_mode{0};
 bool g_init_done = false;
 int g_init_status = NCZ_ERROR_NOT_INITIALIZED;
 std::atomic<uint64_t> g_launches{0};
@@ -385,10 +397,22 @@ int launch_on_current(const Resolved &r, int dev) {
         p.part_o = static_cast<float *>(ws);
         p.part_ml = p.part_o + rows * r.d;
     }
+    // Split-Q items when the launch has no split-KV and too few items of two Q
+    // tiles to keep every SM busy for long.
+    p.qsplit = 0;
+    if (p.num_splits == 1) {
+        const int mode = g_qsplit_mode.load(std::memory_order_relaxed);
+        const size_t pair_items = static_cast<size_t>(p.num_groups) * r.bh;
+        if (mode == 1 || (mode == 0 && pair_items < static_cast<size_t>(NCZ_QSPLIT_ITEMS_PER_SM) *
+                                                        static_cast<size_t>(device_sms(dev))))
+            p.qsplit = 1;
+    }
     // One CTA per work item, heaviest first; at most one is resident per SM (TMEM
     // holds one CTA's 512 columns) and it takes over the items of CTAs that have
     // not started yet.
-    const size_t items = static_cast<size_t>(p.num_groups) * r.bh * static_cast<size_t>(p.num_splits);
+    const size_t n_qt = (r.seq + ncz::kBlockM - 1) / ncz::kBlockM;
+    const size_t items = p.qsplit ? n_qt * r.bh
+                                  : static_cast<size_t>(p.num_groups) * r.bh * static_cast<size_t>(p.num_splits);
     const unsigned grid = static_cast<unsigned>(items);
 #ifdef NCZ_DEBUG_ITEM_VISITS
     p.item_visits = r.item_visits;
@@ -927,6 +951,34 @@ int ncz_test_item_work(size_t batch_heads, size_t seq_len, uint32_t causal, int 
     if (item >= items) return NCZ_ERROR_INVALID_VALUE;
     const ncz::Work wk = ncz::make_work(p, item);
     const int32_t vals[8] = {wk.slice, wk.q_base, wk.split, wk.kv0, wk.n[0], wk.n[1], wk.n_max, p.num_splits};
+    std::memcpy(out, vals, sizeof(vals));
+    return NCZ_SUCCESS;
+}
+
+int ncz_test_set_qsplit(int mode) {
+    if (mode < 0 || mode > 2) return NCZ_ERROR_INVALID_VALUE;
+    g_qsplit_mode.store(mode, std::memory_order_relaxed);
+    return NCZ_SUCCESS;
+}
+
+int ncz_test_qsplit_work(size_t batch_heads, size_t seq_len, uint32_t causal, int chunk_slices, int item,
+                         int32_t *out) {
+    if (out == nullptr || batch_heads == 0 || seq_len == 0 || chunk_slices < 1 || item < 0 ||
+        seq_len > (size_t(1) << 30) || batch_heads > (size_t(1) << 20))
+        return NCZ_ERROR_INVALID_VALUE;
+    FlashParams p{};
+    p.batch_heads = static_cast<int>(batch_heads);
+    p.seq_len = static_cast<int>(seq_len);
+    p.causal = causal != 0;
+    p.num_groups = static_cast<int>((seq_len + kGroupRows - 1) / kGroupRows);
+    p.num_splits = 1;
+    p.kv_per_split = static_cast<int>((seq_len + ncz::kBlockN - 1) / ncz::kBlockN);
+    p.chunk_slices = static_cast<int>(std::min<size_t>(static_cast<size_t>(chunk_slices), batch_heads));
+    p.qsplit = 1;
+    const long long items = static_cast<long long>((seq_len + ncz::kBlockM - 1) / ncz::kBlockM) * p.batch_heads;
+    if (item >= items) return NCZ_ERROR_INVALID_VALUE;
+    const ncz::Work wk = ncz::make_work(p, item);
+    const int32_t vals[6] = {wk.slice, wk.q_base, wk.n[0], wk.n[1], wk.n_max, wk.kstride};
     std::memcpy(out, vals, sizeof(vals));
     return NCZ_SUCCESS;
 }

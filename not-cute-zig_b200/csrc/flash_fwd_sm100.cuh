@@ -117,6 +117,8 @@ enum WaitSite : uint32_t {
     kSiteOFree = 13,
     kSiteClcFull = 14,
     kSiteClcEmpty = 15,
+    kSiteMergeReady = 16,
+    kSiteMergeDone = 17,
 };
 
 struct FlashParams {
@@ -146,6 +148,11 @@ struct FlashParams {
     // heaviest first, before the next chunk), so the K/V a chunk reads stays in
     // L2 while its groups pass over it.
     int chunk_slices;
+    // Split-Q items (for grids too small to fill the GPU): an item is one
+    // 128-row Q tile, whose K tiles alternate between the two pipelines (the
+    // even ones to one, the odd ones to the other); the two online-softmax
+    // states merge in the CTA at the epilogue.  0 = items of two Q tiles.
+    int qsplit;
     float *part_o;
     float *part_ml;
 #ifdef NCZ_DEBUG_ITEM_VISITS
@@ -196,26 +203,46 @@ struct SmemLayout {
     static constexpr int kBarDrain = kBarOFree + kQTiles;  // one per MMA warp
     static constexpr int kBarClcFull = kBarDrain + kQTiles;
     static constexpr int kBarClcEmpty = kBarClcFull + kClcSlots;
-    static constexpr int kNumBars = kBarClcEmpty + kClcSlots;
+    // split-Q epilogue hand-off per SM sub-partition (the two softmax warps of
+    // the same 32 rows): merge_ready[4] (the helper's state is in place),
+    // merge_done[4] (the writer has read it)
+    static constexpr int kBarMergeReady = kBarClcEmpty + kClcSlots;
+    static constexpr int kBarMergeDone = kBarMergeReady + 4;
+    static constexpr int kNumBars = kBarMergeDone + 4;
     static constexpr int kOffClc = (kOffBar + kNumBars * 8 + 15) / 16 * 16;  // 16-byte launch-control responses
     static constexpr int kOffTmemSlot = kOffClc + 16 * kClcSlots;
     static constexpr int kOffAbort = kOffTmemSlot + 4;
     static constexpr int kOffStash = kOffAbort + 4;  // per warp: item walk state (2 ints)
-    static constexpr int kBytes = kOffStash + 8 * (kThreads / 32);
+    static constexpr int kOffMerge = (kOffStash + 8 * (kThreads / 32) + 15) / 16 * 16;  // [4][32] (m, l) pairs
+    static constexpr int kBytes = kOffMerge + 4 * 32 * 8;
     static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
     static_assert(kStages >= 2, "K/V ring");
     static_assert(kAlloc <= 227 * 1024, "shared memory");
 };
 
+// An item as seen by its two pipeline slots p = 0, 1 (pipeline w takes slot
+// w ^ (item count & 1)).  Normally slot p is Q tile p of the item (rows
+// q_base + 128 p ..), visiting K tiles kv0, kv0 + 1, ...; in a split-Q item
+// both slots share Q tile 0 and slot p visits K tiles p, p + 2, p + 4, ...
+// (kstride 2).  Either way slot p's j-th K tile is ring tile j * kstride + p *
+// (kstride - 1) of the item, and the item streams n_max ring tiles in order.
 struct Work {
     int slice;
     int q_base;
     int split;
     int kv0;            // first K tile of this CTA's range
-    int n[kQTiles];     // K/V tiles each Q tile visits in the range (0 = none)
-    int diag[kQTiles];  // last K tile a Q tile sees at all (the only one with masked keys)
-    int n_max;
+    int n[kQTiles];     // K/V tiles slot p visits (0 = none)
+    int diag[kQTiles];  // last K tile slot p's rows see at all (the only one with masked keys)
+    int n_max;          // K/V ring tiles of the item
+    int kstride;        // 1, or 2 for a split-Q item
 };
+
+__host__ __device__ __forceinline__ int slot_qtile(const Work &wk, int slot) { return wk.kstride == 2 ? 0 : slot; }
+// Q tile `tile` (0 or 1) of the item is loaded: some slot reads it.
+__host__ __device__ __forceinline__ bool q_tile_used(const Work &wk, int tile) {
+    return wk.kstride == 2 ? (tile == 0 && wk.n[0] > 0) : wk.n[tile] > 0;
+}
+__host__ __device__ __forceinline__ int slot_koff(const Work &wk, int slot) { return wk.kstride == 2 ? slot : 0; }
 
 __device__ uint32_t g_ncz_status = 0u;
 // Bound of every mbarrier wait, in SM cycles (tests shorten it, ncz_test_set_wait_limit).
@@ -230,6 +257,30 @@ __host__ __device__ constexpr int imin(int a, int b) { return a < b ? a : b; }
 // (ncz_test_item_work).
 __host__ __device__ __forceinline__ Work make_work(const FlashParams &p, int item) {
     Work wk;
+    const int n_kv = (p.seq_len + kBlockN - 1) / kBlockN;
+    if (p.qsplit) {
+        // Chunks of chunk_slices slices; inside a chunk the heaviest (last) Q
+        // tiles first, then slice.  The item's K tiles alternate between the slots.
+        const int n_qt = (p.seq_len + kBlockM - 1) / kBlockM;
+        const int per_chunk = p.chunk_slices * n_qt;
+        const int chunk = item / per_chunk;
+        const int off = item - chunk * per_chunk;
+        const int c0 = chunk * p.chunk_slices;
+        const int slices = imin(p.chunk_slices, p.batch_heads - c0);
+        const int qt = n_qt - 1 - off / slices;
+        wk.slice = c0 + off % slices;
+        wk.split = 0;
+        wk.q_base = qt * kBlockM;
+        wk.kv0 = 0;
+        const int last_row = imin(wk.q_base + kBlockM, p.seq_len) - 1;
+        const int total = p.causal ? last_row / kBlockN + 1 : n_kv;
+        wk.n[0] = (total + 1) / 2;
+        wk.n[1] = total / 2;
+        wk.diag[0] = wk.diag[1] = total - 1;
+        wk.n_max = total;
+        wk.kstride = 2;
+        return wk;
+    }
     // Chunks of chunk_slices slices; inside a chunk the heaviest (last) Q-tile
     // groups first (under causal masking they visit the most K tiles), then
     // slice, then K range.
@@ -245,8 +296,8 @@ __host__ __device__ __forceinline__ Work make_work(const FlashParams &p, int ite
     wk.split = rem % p.num_splits;
     wk.q_base = group * (kQTiles * kBlockM);
     wk.kv0 = wk.split * p.kv_per_split;
-    const int n_kv = (p.seq_len + kBlockN - 1) / kBlockN;
     wk.n_max = 0;
+    wk.kstride = 1;
 #pragma unroll
     for (int w = 0; w < kQTiles; ++w) {
         const int q0 = wk.q_base + w * kBlockM;
@@ -315,6 +366,8 @@ struct Bars {
     __device__ __forceinline__ uint32_t clc_full(int s) const { return at(L::kBarClcFull + s); }
     __device__ __forceinline__ uint32_t clc_empty(int s) const { return at(L::kBarClcEmpty + s); }
     __device__ __forceinline__ uint32_t clc_resp(int s) const { return base + L::kOffClc + 16u * s; }
+    __device__ __forceinline__ uint32_t merge_ready(int sub) const { return at(L::kBarMergeReady + sub); }
+    __device__ __forceinline__ uint32_t merge_done(int sub) const { return at(L::kBarMergeDone + sub); }
 };
 
 // ---------------------------------------------------------------------------
@@ -377,11 +430,11 @@ __device__ __forceinline__ void producer_tma(const FlashParams &p, const CUtenso
         }
         uint32_t qbytes = 0;
 #pragma unroll
-        for (int w = 0; w < kQTiles; ++w) qbytes += wk.n[w] > 0 ? L::kQTile : 0;
+        for (int w = 0; w < kQTiles; ++w) qbytes += q_tile_used(wk, w) ? L::kQTile : 0;
         mbar_arrive_expect_tx_elect(b.q_full(qs), qbytes);
 #pragma unroll
         for (int w = 0; w < kQTiles; ++w)
-            if (wk.n[w] > 0)
+            if (q_tile_used(wk, w))
                 tma_load_3d_elect(sbase + L::kOffQ + qs * L::kQSlot + w * L::kQTile, tq, b.q_full(qs), 0,
                                   wk.q_base + w * kBlockM, wk.slice);
         const int cur = it++;
@@ -478,7 +531,7 @@ __device__ __forceinline__ void producer_lsu(const FlashParams &p, uint8_t *smem
         const int req_at = wk.n_max > kClcLead ? wk.n_max - kClcLead : 0;  // see kClcLead
 #pragma unroll
         for (int w = 0; w < kQTiles; ++w)
-            if (wk.n[w] > 0)
+            if (q_tile_used(wk, w))
                 lsu_tile<D, kBlockM>(smem + L::kOffQ + slot * L::kQSlot + w * L::kQTile, qs, p.q_row,
                                      wk.q_base + w * kBlockM, p.seq_len, lane);
         fence_proxy_async_smem();
@@ -551,14 +604,16 @@ __device__ __forceinline__ void issue_pv(uint32_t t, bool first, uint32_t sbase,
                                       first ? 0u : 1u);
 }
 
-// One MMA warp per Q tile w (warps 1 and 2), over all of the CTA's items.  Per
-// K tile j of an item: QK_w(j+1) as soon as the softmax has read S_w(j) and
-// K(j+1) is resident, then PV_w(j) once P_w(j) is stored and V(j) is resident;
-// the first PV of an item also waits until the softmax has read the previous
-// item's O (o_free).  After its item's last QK the warp counts itself out of
-// the Q slot (q_empty).  Each warp arrives once per K tile on the stage's
-// kv_empty barrier (a commit after its PV, or a plain arrive past its causal
-// range), so a stage is released when both Q tiles are done with it.
+// One MMA warp per pipeline w (warps 1 and 2), over all of the CTA's items.
+// Per K tile j of its slot: QK_w(j+1) as soon as the softmax has read S_w(j)
+// and K(j+1) is resident, then PV_w(j) once P_w(j) is stored and V(j) is
+// resident; the first PV of an item also waits until the softmax has read the
+// previous item's O (o_free).  After its item's last QK the warp counts itself
+// out of the Q slot (q_empty).  Each warp arrives once per ring tile of the
+// item on the stage's kv_empty barrier: a commit after its PV for the tiles its
+// slot visits, a plain arrive for the others (past its causal range, or the
+// other slot's tiles of a split-Q item), issued in ring order as soon as each
+// is loaded, so a stage is released when both pipelines are done with it.
 template <int D, bool kBf16>
 __device__ __forceinline__ void mma_role(const FlashParams &p, int w, uint32_t sbase, uint32_t tmem,
                                          volatile uint32_t *abort_flag, int lane) {
@@ -567,29 +622,46 @@ __device__ __forceinline__ void mma_role(const FlashParams &p, int w, uint32_t s
     const Bars<D> b{sbase};
     const uint32_t tS = tmem + w * kTileCols, tP = tS + kColP, tO = tS + kColO;
     uint32_t t = 0;    // ring tiles passed (all items)
-    uint32_t sc = 0;   // K tiles of this Q tile so far: S/P/O barrier phases
-    uint32_t epi = 0;  // items in which this Q tile had work: o_free phases
+    uint32_t sc = 0;   // K tiles of this pipeline so far: S/P/O barrier phases
+    uint32_t epi = 0;  // items in which this pipeline had work: o_free phases
     bool ok = true, walk = false;
     for (int item = static_cast<int>(blockIdx.x), it = 0; ok && item >= 0;
          ++it, item = ok && walk ? take_item(b, it, abort_flag, lane) : -1) {
         const Work wk = make_work(p, item);
         walk = wk.n_max < p.walk_tiles;
-        const int wq = w ^ (it & 1);  // Q tile of the item this pipeline takes
+        const int wq = w ^ (it & 1);           // slot of the item this pipeline takes
         const int n = wq ? wk.n[1] : wk.n[0];  // a select keeps Work out of local memory
+        const int ks = wk.kstride;
+        const int koff = slot_koff(wk, wq);    // slot's j-th K tile = ring tile koff + j * ks
         const int qs = it & 1;
+        // Ring tiles of the item before `upto` that this slot does not visit:
+        // released on the other pipeline's behalf once loaded, in ring order.
+        int rel = 0;
+        auto release_before = [&](int upto) -> bool {
+            for (; rel < upto; ++rel) {
+                const int dj = rel - koff;
+                if (dj >= 0 && dj % ks == 0 && dj / ks < n) continue;  // one of this slot's tiles
+                const uint32_t tu = t + rel;
+                if (!warp_wait(b.k_full(tu % S), (tu / S) & 1, abort_flag, kSiteKFull)) return false;
+                if (lane == 0) mbar_arrive(b.kv_empty(tu % S));
+                __syncwarp();
+            }
+            return true;
+        };
         // Waited for every item, also without work: this warp's q_empty arrivals
         // then never run two phases ahead of the producer.
         ok = warp_wait(b.q_full(qs), (it >> 1) & 1, abort_flag, kSiteQFull);
         if (!ok) break;
         tc_fence_after();
-        const uint64_t qdesc =
-            umma_smem_desc(sbase + L::kOffQ + qs * L::kQSlot + wq * L::kQTile, 16, 8 * L::kSpan, L::kUmmaLayout);
+        const uint64_t qdesc = umma_smem_desc(sbase + L::kOffQ + qs * L::kQSlot + slot_qtile(wk, wq) * L::kQTile, 16,
+                                              8 * L::kSpan, L::kUmmaLayout);
         if (n > 0) {
-            ok = (sc == 0 || warp_wait(b.s_free(w), (sc - 1) & 1, abort_flag, kSiteSFree)) &&
-                 warp_wait(b.k_full(t % S), (t / S) & 1, abort_flag, kSiteKFull);
+            const uint32_t t0 = t + koff;
+            ok = release_before(koff) && (sc == 0 || warp_wait(b.s_free(w), (sc - 1) & 1, abort_flag, kSiteSFree)) &&
+                 warp_wait(b.k_full(t0 % S), (t0 / S) & 1, abort_flag, kSiteKFull);
             if (!ok) break;
             tc_fence_after();
-            issue_qk<D, kBf16>(t, sbase, tS, qdesc);
+            issue_qk<D, kBf16>(t0, sbase, tS, qdesc);
             if (!(w == 0 && g_ncz_test_drop != 0)) umma_commit_elect(b.s_full(w));
             if (n == 1) umma_commit_elect(b.q_empty(qs));
         } else {
@@ -597,16 +669,17 @@ __device__ __forceinline__ void mma_role(const FlashParams &p, int w, uint32_t s
             if (lane == 0) mbar_arrive(b.q_empty(qs));
             __syncwarp();
         }
-        int j = 0;
-        for (; ok && j < n; ++j) {
-            const uint32_t tj = t + j;
+        for (int j = 0; ok && j < n; ++j) {
+            const uint32_t tj = t + koff + j * ks;
             const int st = tj % S;
             if (j + 1 < n) {
-                ok = warp_wait(b.s_free(w), (sc + j) & 1, abort_flag, kSiteSFree) &&
-                     warp_wait(b.k_full((tj + 1) % S), ((tj + 1) / S) & 1, abort_flag, kSiteKFull);
+                const uint32_t tn = tj + ks;
+                ok = release_before(koff + (j + 1) * ks) &&
+                     warp_wait(b.s_free(w), (sc + j) & 1, abort_flag, kSiteSFree) &&
+                     warp_wait(b.k_full(tn % S), (tn / S) & 1, abort_flag, kSiteKFull);
                 if (!ok) break;
                 tc_fence_after();
-                issue_qk<D, kBf16>(tj + 1, sbase, tS, qdesc);
+                issue_qk<D, kBf16>(tn, sbase, tS, qdesc);
                 umma_commit_elect(b.s_full(w));
                 if (j + 2 == n) umma_commit_elect(b.q_empty(qs));  // the item's last QK
             }
@@ -617,16 +690,9 @@ __device__ __forceinline__ void mma_role(const FlashParams &p, int w, uint32_t s
             tc_fence_after();
             issue_pv<D, kBf16>(tj, j == 0, sbase, tP, tO);
             umma_commit_elect(b.o_done(w));
-            umma_commit_elect(b.kv_empty(st));  // this Q tile is done with K(tj) and V(tj)
+            umma_commit_elect(b.kv_empty(st));  // this pipeline is done with K(tj) and V(tj)
         }
-        // K tiles beyond this Q tile's causal range: release them on its behalf, once
-        // each is loaded (so the arrival counts toward that tile's use of the stage).
-        for (; ok && j < wk.n_max; ++j) {
-            const uint32_t tj = t + j;
-            ok = warp_wait(b.k_full(tj % S), (tj / S) & 1, abort_flag, kSiteKFull);
-            if (ok && lane == 0) mbar_arrive(b.kv_empty(tj % S));
-            __syncwarp();
-        }
+        if (ok) ok = release_before(wk.n_max);  // the item's remaining tiles of the other slot
         if (n > 0) {
             sc += n;
             ++epi;
@@ -886,17 +952,19 @@ __device__ __forceinline__ void softmax_role(const FlashParams &p, uint8_t *smem
     // tile loop runs, so it holds no registers there.
     volatile int *stash = reinterpret_cast<volatile int *>(smem + L::kOffStash + 8 * warp);
     uint32_t ph = 0;  // parity of the K tiles of this pipeline so far (all items): barrier phases
+    uint32_t mc = 0;  // split-Q merges this warp took part in: merge barrier phases
     bool ok = true, walk = false;
     for (int item = static_cast<int>(blockIdx.x), it = 0; ok && item >= 0;
          ++it, item = ok && walk ? take_item(b, it, abort_flag, lane) : -1) {
-        int n, row, kv0, diag;
+        int n, row, kv0, diag, ks;
         {
             const Work wk = make_work(p, item);
             walk = wk.n_max < p.walk_tiles;
-            const int wq = w ^ (it & 1);  // Q tile of the item this pipeline takes
+            const int wq = w ^ (it & 1);  // slot of the item this pipeline takes
             n = wq ? wk.n[1] : wk.n[0];
-            row = wk.q_base + wq * kBlockM + r;
-            kv0 = wk.kv0;
+            row = wk.q_base + slot_qtile(wk, wq) * kBlockM + r;
+            ks = wk.kstride;
+            kv0 = wk.kv0 + slot_koff(wk, wq);  // the slot's j-th K tile is kv0 + j * ks
             diag = wq ? wk.diag[1] : wk.diag[0];
         }
         if (n == 0) {  // no rows of this pipeline in the item: nothing staged in its Q tile
@@ -934,7 +1002,7 @@ __device__ __forceinline__ void softmax_role(const FlashParams &p, uint8_t *smem
             bool half = false;
             float mx;
             if constexpr (decltype(final)::value) {
-                const int jg = kv0 + j;  // K tile index in the sequence
+                const int jg = kv0 + j * ks;  // K tile index in the sequence
                 const bool last = jg == diag;
                 const int lim = lim_of(p, row, jg);
                 // Every key of the upper half masked for all 32 rows of this warp
@@ -1005,18 +1073,67 @@ __device__ __forceinline__ void softmax_role(const FlashParams &p, uint8_t *smem
         item = stash[0];
         it = stash[1];
         const Work wk = make_work(p, item);
+        const int wq = w ^ (it & 1);
+        const bool qsp = wk.kstride == 2;
+        // A split-Q item whose both slots visited K tiles: slot 0's warp writes the
+        // rows, merging slot 1's state (same TMEM lanes, the other pipeline's
+        // columns) into its own: O = (2^(m0-M) O0 + 2^(m1-M) O1) /
+        // (2^(m0-M) l0 + 2^(m1-M) l1), M = max(m0, m1).
+        const bool merge = qsp && wk.n[1] > 0;
+        if (merge && wq == 1) {
+            // Slot 1: hand (m, l) over, and release O only once the writer has read it.
+            reinterpret_cast<float2 *>(smem + L::kOffMerge)[sub * 32 + lane] = make_float2(m, l);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(b.merge_ready(sub));
+            ok = warp_wait(b.merge_done(sub), mc & 1, abort_flag, kSiteMergeDone);
+            ++mc;
+            if (!ok) break;
+            if (lane == 0) {
+                mbar_arrive(b.o_free(w));
+                mbar_arrive(b.q_empty(it & 1));  // nothing staged by this warp
+            }
+            __syncwarp();
+            ph ^= static_cast<uint32_t>(n) & 1u;
+            continue;
+        }
         tc_fence_after();
         float o[D];
         load_cols<D>(tO, o);
-        tc_fence_before();
+        if (merge) {
+            ok = warp_wait(b.merge_ready(sub), mc & 1, abort_flag, kSiteMergeReady);
+            ++mc;
+            if (!ok) break;
+            tc_fence_after();
+            const float2 ml = reinterpret_cast<const float2 *>(smem + L::kOffMerge)[sub * 32 + lane];
+            const float mm = fmaxf(m, ml.x);
+            const float a0 = ex2_approx(m - mm), a1 = ex2_approx(ml.x - mm);
+            const uint32_t tO1 = tmem + (static_cast<uint32_t>(sub * 32) << 16) + (1 - w) * kTileCols + kColO;
+            constexpr int kC = D < 16 ? D : 16;
+#pragma unroll
+            for (int c0 = 0; c0 < D; c0 += kC) {
+                float o1[kC];
+                load_cols<kC>(tO1 + c0, o1);
+#pragma unroll
+                for (int c = 0; c < kC; ++c) o[c0 + c] = o[c0 + c] * a0 + o1[c] * a1;
+            }
+            l = l * a0 + ml.y * a1;
+            m = mm;
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(b.merge_done(sub));
+        } else {
+            tc_fence_before();
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(b.o_free(w));
-        // O goes out through this pipeline's Q tile of the item (its last QK is
-        // done); the producer refills the slot only after every softmax warp
+        // O goes out through shared memory: this pipeline's Q tile of the item
+        // (its last QK is done), or for a split-Q item the slot's unused second
+        // Q tile; the producer refills the slot only after every softmax warp
         // has arrived on q_empty.
-        const int wq = w ^ (it & 1);
-        uint8_t *stage = smem + L::kOffQ + (it & 1) * L::kQSlot + wq * L::kQTile + sub * 32 * L::kSpan;
-        const int row0 = wk.q_base + wq * kBlockM + sub * 32;  // this warp's first row
+        const int stile = qsp ? 1 : wq;
+        uint8_t *stage = smem + L::kOffQ + (it & 1) * L::kQSlot + stile * L::kQTile + sub * 32 * L::kSpan;
+        const int row0 = wk.q_base + slot_qtile(wk, wq) * kBlockM + sub * 32;  // this warp's first row
         const int valid = imin(32, seq_len - row0);
         if (p.num_splits > 1) {
             write_partial_staged<D>(p, wk, row0, row, o, m, l, stage, valid, lane);
@@ -1073,6 +1190,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < kClcSlots; ++c) {
             mbar_init(b.clc_full(c), 1);
             mbar_init(b.clc_empty(c), kClcReaders);  // one arrival per reader warp
+        }
+        for (int q = 0; q < 4; ++q) {
+            mbar_init(b.merge_ready(q), 1);
+            mbar_init(b.merge_done(q), 1);
         }
         *abort_flag = 0u;
         mbar_fence_init();

@@ -78,7 +78,8 @@ def test_one_shard_per_device(ncz, fake):
     ncz.flash.launch_multi([desc(ncz, dev, base=BASE + dev * SPAN) for dev in range(8)])
     assert [x.device for x in fake.launches] == list(range(8))
     assert set(labels(ncz, fake.launches)) == {"flash_fwd<64,tma,f16>"}
-    assert all(x.grid == 4 * 4 and x.block == 384 for x in fake.launches)  # 4 row groups x 4 slices
+    # 4 row groups x 4 slices would leave SMs idle: split-Q items, 8 Q tiles x 4 slices
+    assert all(x.grid == 8 * 4 and x.block == 384 for x in fake.launches)
     assert ncz.flash.launch_count() - before == 8
     assert len(fake.encodes) == 24 and {e[2] for e in fake.encodes} == {128}
     assert fake.current() == 0
@@ -200,7 +201,8 @@ def test_host_pipeline_copies_and_copy_failure(ncz, fake):
     n = 1024 * 64
     x = desc(ncz, 1, bh=16, seq=1024)
     assert fwd_host(ncz, x, 4) == 0
-    assert [l.device for l in fake.launches] == [1] * 4 and all(l.grid == 16 for l in fake.launches)
+    # each 4-slice chunk: 16 items of two Q tiles would leave SMs idle, so 8 Q tiles x 4 slices
+    assert [l.device for l in fake.launches] == [1] * 4 and all(l.grid == 32 for l in fake.launches)
     up = [c for c in fake.copies if c[1] == ncz.driver.COPY_HOST_TO_DEVICE]
     down = [c for c in fake.copies if c[1] == ncz.driver.COPY_DEVICE_TO_HOST]
     assert len(up) == 12 and sum(c[2] for c in up) == 3 * 16 * n * 2

@@ -221,11 +221,14 @@ def test_repeated_launches_are_bit_identical(ncz, oracle_mod, d):
 
 @pytest.mark.parametrize("chunk", [0, 1, 3, 7, 64])
 @pytest.mark.parametrize("o_dtype", ["float32", "float16"])
-def test_host_pipeline_matches_device_launch(ncz, oracle_mod, chunk, o_dtype):
+def test_host_pipeline_matches_device_launch(ncz, oracle_mod, qsplit_mode, chunk, o_dtype):
     """ncz_flash_fwd_host (chunked upload / forward / download on three streams)
-    gives exactly the device-path result, for chunk sizes that do and do not
+    gives exactly the device-path result (with items of two Q tiles in every
+    launch: a small chunk would otherwise take split-Q items, which sum in
+    another order), for chunk sizes that do and do not
     divide batch_heads, with padded slice strides (the last chunk copies only up
     to its last row)."""
+    qsplit_mode(2)
     bh, s, d = 7, 333, 64
     strides = (s * d + 24, s * d + 40, s * d + 8, s * d + 16)
     p = C.normal_problem(bh, s, d, True, 61, oracle_mod, std=0.7, strides=strides)
@@ -500,9 +503,12 @@ def test_compare_harness_multi_device(ncz):
     assert rec["mean_ms"] >= max(rec["device_ms"]) - 1e-6  # the slowest device per iteration
 
 
-def test_host_pipeline_tapered_default_matches_device_launch(ncz, oracle_mod):
+def test_host_pipeline_tapered_default_matches_device_launch(ncz, oracle_mod, qsplit_mode):
     """bh=96, S=1024: the default plan tapers (3, 6, 12 x 6, 6, 6, 3 slices); the
-    result equals the device path bit for bit."""
+    result equals the device path bit for bit (items of two Q tiles in every
+    launch), and with the automatic item kinds (split-Q in the small chunks)
+    it meets the parity bound."""
+    qsplit_mode(2)
     bh, s, d = 96, 1024, 64
     p = C.normal_problem(bh, s, d, True, 67, oracle_mod, std=0.7)
     dev = torch.device("cuda:0")
@@ -519,6 +525,11 @@ def test_host_pipeline_tapered_default_matches_device_launch(ncz, oracle_mod):
     assert ncz.flash.launch_count() - before == 11
     assert ncz.sync_status() == 0
     assert torch.equal(oh, o_ref.cpu())
+    qsplit_mode(0)
+    ncz.launch_host(qh, kh, vh, oh, qd, kd, vd, od, opts)
+    torch.cuda.synchronize()
+    assert ncz.sync_status() == 0
+    C.check(oh.numpy(), C.reference(p, oracle_mod), C.active_index(p), "host pipeline, automatic item kinds")
 
 
 def _run_bf16(ncz, p, o_dtype=torch.float32, producer="auto", splits=None):
@@ -621,3 +632,53 @@ def test_item_walk_lsu_equals_tma(ncz, oracle_mod):
     b = run(ncz, p, producer="lsu")
     C.check(a, C.reference(p, oracle_mod), C.active_index(p), "item walk, TMA producer")
     assert np.array_equal(a, b)
+
+
+QSPLIT_CASES = [(8, 1024, 64, True), (3, 1000, 64, False), (2, 129, 32, True), (5, 100, 16, True),
+                (4, 777, 64, True), (1, 4096, 32, True), (300, 600, 64, True)]
+
+
+@pytest.fixture
+def qsplit_mode(ncz):
+    """Sets the split-Q choice for one test and restores the automatic one."""
+    lib = ncz.flash.lib()
+
+    def set_mode(mode):
+        assert lib.ncz_test_set_qsplit(mode) == 0
+
+    yield set_mode
+    assert lib.ncz_test_set_qsplit(0) == 0
+
+
+@pytest.mark.parametrize("case", QSPLIT_CASES, ids=lambda c: f"bh{c[0]}_s{c[1]}_d{c[2]}_c{int(c[3])}")
+def test_split_q_items_match_oracle(ncz, oracle_mod, qsplit_mode, case):
+    """Split-Q items (one Q tile per item, its K tiles alternating between the
+    two pipelines, states merged in the CTA) against the oracle, next to items
+    of two Q tiles; nothing outside the active rows written.  bh=300, S=600
+    gives 1500 items walked by 148 CTAs (merge barriers over many items)."""
+    bh, s, d, causal = case
+    p = C.normal_problem(bh, s, d, causal, 83, oracle_mod, std=0.8)
+    want = C.reference(p, oracle_mod)
+    idx = C.active_index(p)
+    for mode in (1, 2):
+        qsplit_mode(mode)
+        got = run(ncz, p)
+        C.check(got, want, idx, f"split-Q mode {mode} {case}")
+        assert untouched(got, p, idx)
+
+
+def test_split_q_producers_and_output_types(ncz, oracle_mod, qsplit_mode):
+    """Split-Q with the plain-load producer (bit-identical to TMA), f16 O and
+    bf16 inputs."""
+    qsplit_mode(1)
+    p = C.normal_problem(3, 555, 64, True, 89, oracle_mod, std=0.7)
+    want = C.reference(p, oracle_mod)
+    idx = C.active_index(p)
+    a = run(ncz, p, producer="tma")
+    b = run(ncz, p, producer="lsu")
+    assert np.array_equal(a, b)
+    C.check(a, want, idx, "split-Q tma")
+    C.check(run(ncz, p, o_dtype="float16"), want, idx, "split-Q f16 O", o_unit=2.0 ** -11)
+    pb = C.normal_problem_bf16(2, 700, 32, True, 97, oracle_mod, std=0.7)
+    C.check(_run_bf16(ncz, pb), C.reference(pb, oracle_mod), C.active_index(pb), "split-Q bf16",
+            atol=C.ATOL_BF16, p_unit=C.P_UNIT_BF16)

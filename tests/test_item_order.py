@@ -61,3 +61,54 @@ def check_item_order(lib, bh, s, causal, splits, chunk):
     assert len(seen) == items
     out = (ctypes.c_int32 * 8)()
     assert lib.ncz_test_item_work(bh, s, int(causal), splits, chunk, items, out) != 0  # past the end
+
+
+def qsplit_work(lib, bh, s, causal, chunk, i):
+    out = (ctypes.c_int32 * 6)()
+    assert lib.ncz_test_qsplit_work(bh, s, int(causal), chunk, i, out) == 0
+    return list(out)
+
+
+@pytest.mark.parametrize("bh,s,causal,chunk", [
+    (8, 1024, True, 8),        # config 2
+    (8, 8192, True, 16),       # config 4 on 8 GPUs
+    (20, 8192, True, 16),      # short last chunk
+    (3, 1000, False, 2),       # ragged S
+    (5, 100, True, 5),         # one Q tile: one K tile, the second slot empty
+    (2, 129, True, 1),
+])
+def test_split_q_item_order(ncz, bh, s, causal, chunk):
+    """Split-Q launches (one Q tile per item): every (slice, Q tile) once,
+    chunks of slices in order, heaviest Q tile first inside a chunk; the item
+    streams all K tiles of its Q tile (up to the causal diagonal) and its two
+    slots take the even (ceil half) and the odd (floor half) of them."""
+    lib = ncz.flash.lib()
+    n_qt = math.ceil(s / 128)
+    n_kv = math.ceil(s / 128)
+    items = n_qt * bh
+    chunk = min(chunk, bh)
+    seen = set()
+    prev_chunk, prev_qt = -1, None
+    for i in range(items):
+        sl, q_base, n0, n1, nmax, kstride = qsplit_work(lib, bh, s, causal, chunk, i)
+        assert kstride == 2 and q_base % 128 == 0 and 0 <= q_base < s and 0 <= sl < bh
+        key = (sl, q_base)
+        assert key not in seen
+        seen.add(key)
+        c, qt = sl // chunk, q_base // 128
+        assert c >= prev_chunk
+        if c == prev_chunk:
+            assert qt <= prev_qt
+        prev_chunk, prev_qt = c, qt
+        total = (min(q_base + 128, s) - 1) // 128 + 1 if causal else n_kv
+        assert nmax == total and n0 == (total + 1) // 2 and n1 == total // 2
+    assert len(seen) == items
+    out = (ctypes.c_int32 * 6)()
+    assert lib.ncz_test_qsplit_work(bh, s, int(causal), chunk, items, out) != 0
+
+
+def test_split_q_mode_hook(ncz):
+    lib = ncz.flash.lib()
+    assert lib.ncz_test_set_qsplit(3) != 0 and lib.ncz_test_set_qsplit(-1) != 0
+    for mode in (1, 2, 0):
+        assert lib.ncz_test_set_qsplit(mode) == 0

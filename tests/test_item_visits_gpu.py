@@ -47,6 +47,30 @@ def debug_lib():
 
 @pytest.mark.parametrize("case", CASES, ids=lambda c: f"bh{c[0]}_s{c[1]}_d{c[2]}_{c[4]}_split{c[6]}")
 def test_every_item_started_exactly_once(ncz, debug_lib, case):
+    check_items(ncz, debug_lib, case)
+
+
+QSPLIT_CASES = [  # split-Q items forced in both libraries
+    (64, 2048, 64, True, "tma", torch.float16, 0),    # 1024 items of one Q tile
+    (300, 600, 32, False, "lsu", torch.float16, 0),   # 1500 items, plain-load producer
+]
+
+
+@pytest.mark.parametrize("case", QSPLIT_CASES, ids=lambda c: f"qsplit_bh{c[0]}_s{c[1]}_d{c[2]}_{c[4]}")
+def test_split_q_items_started_exactly_once(ncz, debug_lib, case):
+    """The same check with split-Q items: each CTA's two pipelines share one Q
+    tile per item and merge their states through barriers whose phases run
+    over all the items a CTA walks."""
+    lib = ncz.flash.lib()
+    debug_lib.ncz_test_set_qsplit.argtypes = [ctypes.c_int]
+    assert lib.ncz_test_set_qsplit(1) == 0 and debug_lib.ncz_test_set_qsplit(1) == 0
+    try:
+        check_items(ncz, debug_lib, case)
+    finally:
+        assert lib.ncz_test_set_qsplit(0) == 0 and debug_lib.ncz_test_set_qsplit(0) == 0
+
+
+def check_items(ncz, debug_lib, case):
     bh, s, d, causal, producer, in_dtype, splits = case
     g = torch.Generator(device="cuda")
     g.manual_seed(bh * 7 + s)

@@ -63,7 +63,7 @@ def test_guards_and_errors(ncz, fake):
     assert status(ncz, st) == "InvalidValue"
     assert fake.launches == []
     assert named(ncz, "flash_attention_fwd_h64_causal", causal=0) == 0
-    assert len(fake.launches) == 1 and fake.launches[0].grid == 4 * 4
+    assert len(fake.launches) == 1 and fake.launches[0].grid == 8 * 4  # split-Q items: 8 Q tiles x 4 slices
 
 
 def test_python_mirror_checks_tensors(ncz):
