@@ -253,20 +253,36 @@ int ncz_test_chunk_plan(size_t batch_heads, size_t chunk_slices, int taper, size
 int ncz_test_item_work(size_t batch_heads, size_t seq_len, uint32_t causal, int splits, int chunk_slices, int item,
                        int32_t *out);
 
-/* Test hook: the work item `item` of a launch of split-Q items (one 128-row
- * Q tile per item, its K tiles alternating between the CTA's two pipelines;
- * the library uses them when a launch without split-KV has too few items of
- * two Q tiles to keep the SMs busy).  out[0..5] = slice, first Q row, K tiles
- * of slot 0 (the even ones), of slot 1 (the odd ones), the item's K tiles,
- * K tile stride (2).  Host only; NCZ_ERROR_INVALID_VALUE past the launch. */
-int ncz_test_qsplit_work(size_t batch_heads, size_t seq_len, uint32_t causal, int chunk_slices, int item,
-                         int32_t *out);
+/* Test hook: the work item `item` of a launch whose top `split_groups` groups
+ * of two 128-row Q tiles (1 .. all of them; the heaviest under causal
+ * masking) run as split-Q items: one Q tile per item, its K tiles alternating
+ * between the CTA's two pipelines.  Those come first in each chunk of
+ * `chunk_slices` slices, heaviest Q tile first, then the other groups' items
+ * of two Q tiles, heaviest group first.  out[0..5] = slice, first Q row, K
+ * tiles of slot 0, of slot 1, the item's K tiles, K tile stride (2 for a
+ * split-Q item, 1 otherwise).  Host only; NCZ_ERROR_INVALID_VALUE past the
+ * launch. */
+int ncz_test_qsplit_work(size_t batch_heads, size_t seq_len, uint32_t causal, int chunk_slices, int split_groups,
+                         int item, int32_t *out);
+
+/* Test hook: the split-Q plan of a launch without split-KV on `sms` SMs:
+ * out[0] = groups run as split-Q items (all of them when the items of two Q
+ * tiles number fewer than 1.25 per SM, else 0), out[1] = the launch's work
+ * items.  Host only. */
+int ncz_test_qsplit_plan(size_t batch_heads, size_t seq_len, size_t sms, int32_t *out);
 
 /* Test hook: the split-Q choice of every following launch of this process:
  * 0 automatic (the default), 1 whenever the launch has no split-KV, 2 never.
  * Results agree either way within the parity bound; the hook lets tests run
  * both item kinds on the same shape. */
 int ncz_test_set_qsplit(int mode);
+
+/* groups >= 0: every following launch without split-KV runs the Q tiles of
+ * its top `groups` Q-tile groups (clamped to the launch's groups) as split-Q
+ * items and the rest as items of two Q tiles, whatever ncz_test_set_qsplit
+ * chose; -1 (the default) hands the choice back to that mode.  Tests and
+ * timing sweeps use it to run one shape under every mix of item kinds. */
+int ncz_test_set_qsplit_groups(int groups);
 
 /* Bound of every in-kernel mbarrier wait on `device` (-1 = current), in SM
  * cycles; 0 restores the default (4e9, about 2 s).  A test shortens it so an

@@ -53,19 +53,26 @@ constexpr int kVariants = 12;  // (D in 16/32/64) x (TMA, LSU) x (f16, bf16 inpu
 #define NCZ_WALK_TILES (1 << 30)
 #endif
 // Split-Q items (one Q tile per item, its K tiles alternating between the two
-// pipelines) when the items of two Q tiles number fewer than this many per SM:
-// some SMs would idle and the longest item bounds the launch, so halving it
-// pays (config 2, 32 items: 22.7 -> 18.1 us).  With more items split-Q lost
-// 9-12 % (each K/V tile then feeds one pipeline instead of two, and there are
-// twice the items), so it stays off there.
+// pipelines) for every Q tile when the items of two Q tiles number fewer than
+// this many per SM: some SMs would idle, or take a second item while the rest
+// finish, and the longest item bounds the launch, so halving it pays (config
+// 2, 32 items: 22.9 -> 18.4 us; 160 causal items at S=8192: 104.5 -> 81.8 us).
+// From 1.5 items per SM up split-Q lost 4-14 %: each K/V tile then feeds one
+// pipeline instead of two (a split-Q K tile costs about 1.4 two-tile steps)
+// and the longest two-tile item no longer bounds the launch.  Splitting only
+// the heaviest groups never gained more than 3 % over the better of none and
+// all in a sweep of 12 shapes, so the plan is all or nothing.
 #ifndef NCZ_QSPLIT_ITEMS_PER_SM
-#define NCZ_QSPLIT_ITEMS_PER_SM 1
+#define NCZ_QSPLIT_ITEMS_PER_SM 1.25
 #endif
 
 std::mutex g_mu;
 // Split-Q choice: 0 automatic, 1 whenever the launch has no split-KV, 2 never
 // (ncz_test_set_qsplit).
 std::atomic<int> g_qsplit_mode{0};
+// >= 0: that many split-Q groups (clamped) instead of the mode's choice
+// (ncz_test_set_qsplit_groups); -1 = the mode decides.
+std::atomic<int> g_qsplit_force{-1};
 bool g_init_done = false;
 int g_init_status = NCZ_ERROR_NOT_INITIALIZED;
 std::atomic<uint64_t> g_launches{0};
@@ -317,6 +324,24 @@ void split_plan(size_t bh, size_t seq, int requested, size_t sms, int *splits, i
     *splits = (n_kv + per - 1) / per;
 }
 
+// Groups (of two 128-row Q tiles) of a launch without split-KV whose Q tiles
+// run as split-Q items: all of them when the items of two Q tiles number fewer
+// than NCZ_QSPLIT_ITEMS_PER_SM per SM, else none.  (Launches with a smaller
+// count, counted from the top group, run through ncz_test_set_qsplit_groups.)
+int qsplit_plan(size_t bh, size_t seq, size_t sms) {
+    const size_t groups = (seq + kGroupRows - 1) / kGroupRows;
+    const double items = static_cast<double>(groups * bh);
+    return items < (NCZ_QSPLIT_ITEMS_PER_SM) * static_cast<double>(sms) ? static_cast<int>(groups) : 0;
+}
+
+// Work items of a launch with `split_groups` split-Q groups (no split-KV).
+size_t qsplit_items(size_t bh, size_t seq, int split_groups) {
+    const size_t groups = (seq + kGroupRows - 1) / kGroupRows;
+    const size_t n_qt = (seq + ncz::kBlockM - 1) / ncz::kBlockM;
+    const size_t low = groups - static_cast<size_t>(split_groups);
+    return bh * (n_qt - ncz::kQTiles * low + low);
+}
+
 void choose_splits(const Resolved &r, int dev, int *splits, int *per_split) {
     split_plan(r.bh, r.seq, r.splits, r.splits == 0 ? static_cast<size_t>(device_sms(dev)) : 0, splits, per_split);
 }
@@ -397,22 +422,25 @@ int launch_on_current(const Resolved &r, int dev) {
         p.part_o = static_cast<float *>(ws);
         p.part_ml = p.part_o + rows * r.d;
     }
-    // Split-Q items when the launch has no split-KV and too few items of two Q
-    // tiles to keep every SM busy for long.
-    p.qsplit = 0;
+    // Split-Q items (launches without split-KV only): for every group when the
+    // items of two Q tiles leave SMs idle, else for the causal groups whose
+    // items are longer than an even share of the work (qsplit_plan).
+    p.qsplit_groups = 0;
     if (p.num_splits == 1) {
         const int mode = g_qsplit_mode.load(std::memory_order_relaxed);
-        const size_t pair_items = static_cast<size_t>(p.num_groups) * r.bh;
-        if (mode == 1 || (mode == 0 && pair_items < static_cast<size_t>(NCZ_QSPLIT_ITEMS_PER_SM) *
-                                                        static_cast<size_t>(device_sms(dev))))
-            p.qsplit = 1;
+        const int force = g_qsplit_force.load(std::memory_order_relaxed);
+        if (force >= 0)
+            p.qsplit_groups = std::min(force, p.num_groups);
+        else if (mode == 1)
+            p.qsplit_groups = p.num_groups;
+        else if (mode == 0)
+            p.qsplit_groups = qsplit_plan(r.bh, r.seq, static_cast<size_t>(device_sms(dev)));
     }
     // One CTA per work item, heaviest first; at most one is resident per SM (TMEM
     // holds one CTA's 512 columns) and it takes over the items of CTAs that have
     // not started yet.
-    const size_t n_qt = (r.seq + ncz::kBlockM - 1) / ncz::kBlockM;
-    const size_t items = p.qsplit ? n_qt * r.bh
-                                  : static_cast<size_t>(p.num_groups) * r.bh * static_cast<size_t>(p.num_splits);
+    const size_t items = p.qsplit_groups > 0 ? qsplit_items(r.bh, r.seq, p.qsplit_groups)
+                                             : static_cast<size_t>(p.num_groups) * r.bh * static_cast<size_t>(p.num_splits);
     const unsigned grid = static_cast<unsigned>(items);
 #ifdef NCZ_DEBUG_ITEM_VISITS
     p.item_visits = r.item_visits;
@@ -961,8 +989,14 @@ int ncz_test_set_qsplit(int mode) {
     return NCZ_SUCCESS;
 }
 
-int ncz_test_qsplit_work(size_t batch_heads, size_t seq_len, uint32_t causal, int chunk_slices, int item,
-                         int32_t *out) {
+int ncz_test_set_qsplit_groups(int groups) {
+    if (groups < -1) return NCZ_ERROR_INVALID_VALUE;
+    g_qsplit_force.store(groups, std::memory_order_relaxed);
+    return NCZ_SUCCESS;
+}
+
+int ncz_test_qsplit_work(size_t batch_heads, size_t seq_len, uint32_t causal, int chunk_slices, int split_groups,
+                         int item, int32_t *out) {
     if (out == nullptr || batch_heads == 0 || seq_len == 0 || chunk_slices < 1 || item < 0 ||
         seq_len > (size_t(1) << 30) || batch_heads > (size_t(1) << 20))
         return NCZ_ERROR_INVALID_VALUE;
@@ -971,15 +1005,23 @@ int ncz_test_qsplit_work(size_t batch_heads, size_t seq_len, uint32_t causal, in
     p.seq_len = static_cast<int>(seq_len);
     p.causal = causal != 0;
     p.num_groups = static_cast<int>((seq_len + kGroupRows - 1) / kGroupRows);
+    if (split_groups < 1 || split_groups > p.num_groups) return NCZ_ERROR_INVALID_VALUE;
     p.num_splits = 1;
     p.kv_per_split = static_cast<int>((seq_len + ncz::kBlockN - 1) / ncz::kBlockN);
     p.chunk_slices = static_cast<int>(std::min<size_t>(static_cast<size_t>(chunk_slices), batch_heads));
-    p.qsplit = 1;
-    const long long items = static_cast<long long>((seq_len + ncz::kBlockM - 1) / ncz::kBlockM) * p.batch_heads;
-    if (item >= items) return NCZ_ERROR_INVALID_VALUE;
+    p.qsplit_groups = split_groups;
+    if (static_cast<size_t>(item) >= qsplit_items(batch_heads, seq_len, split_groups)) return NCZ_ERROR_INVALID_VALUE;
     const ncz::Work wk = ncz::make_work(p, item);
     const int32_t vals[6] = {wk.slice, wk.q_base, wk.n[0], wk.n[1], wk.n_max, wk.kstride};
     std::memcpy(out, vals, sizeof(vals));
+    return NCZ_SUCCESS;
+}
+
+int ncz_test_qsplit_plan(size_t batch_heads, size_t seq_len, size_t sms, int32_t *out) {
+    if (out == nullptr || batch_heads == 0 || seq_len == 0 || sms == 0) return NCZ_ERROR_INVALID_VALUE;
+    out[0] = qsplit_plan(batch_heads, seq_len, sms);
+    out[1] = out[0] > 0 ? static_cast<int32_t>(qsplit_items(batch_heads, seq_len, out[0]))
+                        : static_cast<int32_t>(((seq_len + kGroupRows - 1) / kGroupRows) * batch_heads);
     return NCZ_SUCCESS;
 }
 

@@ -148,11 +148,13 @@ struct FlashParams {
     // heaviest first, before the next chunk), so the K/V a chunk reads stays in
     // L2 while its groups pass over it.
     int chunk_slices;
-    // Split-Q items (for grids too small to fill the GPU): an item is one
-    // 128-row Q tile, whose K tiles alternate between the two pipelines (the
-    // even ones to one, the odd ones to the other); the two online-softmax
-    // states merge in the CTA at the epilogue.  0 = items of two Q tiles.
-    int qsplit;
+    // Split-Q items: an item is one 128-row Q tile, whose K tiles alternate
+    // between the two pipelines (the even ones to one, the odd ones to the
+    // other); the two online-softmax states merge in the CTA at the epilogue.
+    // The Q tiles of the top qsplit_groups Q-tile groups (the heaviest under
+    // causal masking; all groups when it equals num_groups) run as split-Q
+    // items, the other groups as items of two Q tiles.  0 = none.
+    int qsplit_groups;
     float *part_o;
     float *part_ml;
 #ifdef NCZ_DEBUG_ITEM_VISITS
@@ -258,27 +260,57 @@ __host__ __device__ constexpr int imin(int a, int b) { return a < b ? a : b; }
 __host__ __device__ __forceinline__ Work make_work(const FlashParams &p, int item) {
     Work wk;
     const int n_kv = (p.seq_len + kBlockN - 1) / kBlockN;
-    if (p.qsplit) {
-        // Chunks of chunk_slices slices; inside a chunk the heaviest (last) Q
-        // tiles first, then slice.  The item's K tiles alternate between the slots.
+    if (p.qsplit_groups > 0) {
+        // Chunks of chunk_slices slices; inside a chunk the items by K tiles
+        // per pipeline, heaviest first: the items of two Q tiles that visit
+        // more K tiles than the heaviest split-Q item gives each pipeline
+        // (lead groups, heaviest group first, then slice), then the split-Q
+        // items (the Q tiles of the top qsplit_groups groups, heaviest first,
+        // then slice), then the other items of two Q tiles.  No split-KV here.
+        static_assert(kBlockM == kBlockN, "lead groups count K tiles as Q tiles");
         const int n_qt = (p.seq_len + kBlockM - 1) / kBlockM;
-        const int per_chunk = p.chunk_slices * n_qt;
+        const int low_groups = p.num_groups - p.qsplit_groups;  // groups of two-Q-tile items
+        const int split_qt = n_qt - kQTiles * low_groups;       // split-Q items per slice
+        // A low group g is whole and its heavier Q tile visits kQTiles*(g+1)
+        // K tiles under causal masking, n_kv without; the heaviest split-Q item
+        // gives a pipeline (n_kv + 1) / 2.
+        const int lead = p.causal ? low_groups - imin(low_groups, ((n_kv + 1) / 2) / kQTiles) : low_groups;
+        const int per_chunk = p.chunk_slices * (split_qt + low_groups);
         const int chunk = item / per_chunk;
         const int off = item - chunk * per_chunk;
         const int c0 = chunk * p.chunk_slices;
         const int slices = imin(p.chunk_slices, p.batch_heads - c0);
-        const int qt = n_qt - 1 - off / slices;
-        wk.slice = c0 + off % slices;
         wk.split = 0;
-        wk.q_base = qt * kBlockM;
         wk.kv0 = 0;
-        const int last_row = imin(wk.q_base + kBlockM, p.seq_len) - 1;
-        const int total = p.causal ? last_row / kBlockN + 1 : n_kv;
-        wk.n[0] = (total + 1) / 2;
-        wk.n[1] = total / 2;
-        wk.diag[0] = wk.diag[1] = total - 1;
-        wk.n_max = total;
-        wk.kstride = 2;
+        if (off >= slices * lead && off < slices * (lead + split_qt)) {
+            const int rel = off - slices * lead;
+            const int qt = n_qt - 1 - rel / slices;
+            wk.slice = c0 + rel % slices;
+            wk.q_base = qt * kBlockM;
+            const int last_row = imin(wk.q_base + kBlockM, p.seq_len) - 1;
+            const int total = p.causal ? last_row / kBlockN + 1 : n_kv;
+            wk.n[0] = (total + 1) / 2;
+            wk.n[1] = total / 2;
+            wk.diag[0] = wk.diag[1] = total - 1;
+            wk.n_max = total;
+            wk.kstride = 2;
+            return wk;
+        }
+        const int rem = off < slices * lead ? off : off - slices * split_qt;  // place among the two-tile items
+        const int group = low_groups - 1 - rem / slices;
+        wk.slice = c0 + rem % slices;
+        wk.q_base = group * (kQTiles * kBlockM);
+        wk.n_max = 0;
+        wk.kstride = 1;
+#pragma unroll
+        for (int w = 0; w < kQTiles; ++w) {
+            const int q0 = wk.q_base + w * kBlockM;
+            const int last_row = imin(q0 + kBlockM, p.seq_len) - 1;
+            const int total = q0 >= p.seq_len ? 0 : (p.causal ? last_row / kBlockN + 1 : n_kv);
+            wk.n[w] = total;
+            wk.diag[w] = total - 1;
+            wk.n_max = total > wk.n_max ? total : wk.n_max;
+        }
         return wk;
     }
     // Chunks of chunk_slices slices; inside a chunk the heaviest (last) Q-tile

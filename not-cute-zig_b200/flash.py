@@ -121,8 +121,10 @@ _SIGNATURES = {
     "ncz_flash_sync_status": (ctypes.c_int, [ctypes.c_int, _VP, ctypes.POINTER(ctypes.c_uint32)]),
     "ncz_test_set_wait_limit": (ctypes.c_int, [ctypes.c_int, ctypes.c_uint64]),
     "ncz_test_set_qsplit": (ctypes.c_int, [ctypes.c_int]),
-    "ncz_test_qsplit_work": (ctypes.c_int, [_SZ, _SZ, ctypes.c_uint32, ctypes.c_int, ctypes.c_int,
+    "ncz_test_set_qsplit_groups": (ctypes.c_int, [ctypes.c_int]),
+    "ncz_test_qsplit_work": (ctypes.c_int, [_SZ, _SZ, ctypes.c_uint32, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                             ctypes.POINTER(ctypes.c_int32)]),
+    "ncz_test_qsplit_plan": (ctypes.c_int, [_SZ, _SZ, _SZ, ctypes.POINTER(ctypes.c_int32)]),
     "ncz_test_drop_arrive": (ctypes.c_int, [ctypes.c_int, ctypes.c_int]),
     "ncz_test_item_work": (ctypes.c_int, [_SZ, _SZ, ctypes.c_uint32, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                           ctypes.POINTER(ctypes.c_int32)]),

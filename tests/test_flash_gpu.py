@@ -4,6 +4,7 @@ Every launch goes through the reference-shaped Python mirror
 (not-cute-zig_b200.flash.launch / launch_ex -> libncz_flash.so).  Inputs are
 generated on the host, so the kernel and the oracle read identical f16 bits.
 """
+import ctypes
 import math
 
 import numpy as np
@@ -682,3 +683,27 @@ def test_split_q_producers_and_output_types(ncz, oracle_mod, qsplit_mode):
     pb = C.normal_problem_bf16(2, 700, 32, True, 97, oracle_mod, std=0.7)
     C.check(_run_bf16(ncz, pb), C.reference(pb, oracle_mod), C.active_index(pb), "split-Q bf16",
             atol=C.ATOL_BF16, p_unit=C.P_UNIT_BF16)
+
+
+def test_mixed_split_q_and_two_tile_items(ncz, oracle_mod, qsplit_mode):
+    """bh=5, S=8192, causal, the top 15 of 32 groups forced to split-Q items
+    and the rest run as items of two Q tiles in one launch (two-tile items
+    heavier than the heaviest split-Q item first, then the split-Q items, then
+    the lighter two-tile items).  Slices 0 and 4 against the oracle, next to
+    the automatic plan (every group split: 160 two-tile items are fewer than
+    1.25 per SM) and to two-tile items only."""
+    lib = ncz.flash.lib()
+    out = (ctypes.c_int32 * 2)()
+    assert lib.ncz_test_qsplit_plan(5, 8192, 148, out) == 0 and out[0] == 32
+    p = C.normal_problem(5, 8192, 64, True, 101, oracle_mod, std=1.0, k_mul=2.0)
+    want = C.reference(p, oracle_mod, slices=[0, 4])
+    idx = C.active_index(p, slices=[0, 4])
+    assert lib.ncz_test_set_qsplit_groups(15) == 0
+    try:
+        C.check(run(ncz, p), want, idx, "mixed split-Q items")
+    finally:
+        assert lib.ncz_test_set_qsplit_groups(-1) == 0
+    qsplit_mode(0)
+    C.check(run(ncz, p), want, idx, "automatic plan")
+    qsplit_mode(2)
+    C.check(run(ncz, p), want, idx, "two-tile items only")

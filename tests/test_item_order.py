@@ -63,48 +63,96 @@ def check_item_order(lib, bh, s, causal, splits, chunk):
     assert lib.ncz_test_item_work(bh, s, int(causal), splits, chunk, items, out) != 0  # past the end
 
 
-def qsplit_work(lib, bh, s, causal, chunk, i):
+def qsplit_work(lib, bh, s, causal, chunk, groups, i):
     out = (ctypes.c_int32 * 6)()
-    assert lib.ncz_test_qsplit_work(bh, s, int(causal), chunk, i, out) == 0
+    assert lib.ncz_test_qsplit_work(bh, s, int(causal), chunk, groups, i, out) == 0
     return list(out)
 
 
-@pytest.mark.parametrize("bh,s,causal,chunk", [
-    (8, 1024, True, 8),        # config 2
-    (8, 8192, True, 16),       # config 4 on 8 GPUs
-    (20, 8192, True, 16),      # short last chunk
-    (3, 1000, False, 2),       # ragged S
-    (5, 100, True, 5),         # one Q tile: one K tile, the second slot empty
-    (2, 129, True, 1),
+def k_tiles(q_base, s, causal):
+    """K tiles a Q tile starting at q_base visits (reference tile_end)."""
+    if q_base >= s:
+        return 0
+    return (min(q_base + 128, s) - 1) // 128 + 1 if causal else math.ceil(s / 128)
+
+
+@pytest.mark.parametrize("bh,s,causal,chunk,groups", [
+    (8, 1024, True, 8, 4),       # config 2: every group split
+    (8, 8192, True, 16, 4),      # config 4 on 8 GPUs: the top 4 of 32 groups split
+    (8, 8192, True, 16, 32),
+    (20, 8192, True, 16, 3),     # short last chunk
+    (3, 1000, False, 2, 4),      # ragged S, all split
+    (3, 1000, False, 2, 1),      # ragged S: the top group has one Q tile
+    (5, 100, True, 5, 1),        # one Q tile: one K tile, the second slot empty
+    (2, 129, True, 1, 1),
 ])
-def test_split_q_item_order(ncz, bh, s, causal, chunk):
-    """Split-Q launches (one Q tile per item): every (slice, Q tile) once,
-    chunks of slices in order, heaviest Q tile first inside a chunk; the item
-    streams all K tiles of its Q tile (up to the causal diagonal) and its two
-    slots take the even (ceil half) and the odd (floor half) of them."""
+def test_split_q_item_order(ncz, bh, s, causal, chunk, groups):
+    """Launches with split-Q items for the top `groups` groups: every Q tile of
+    those groups is one split-Q item (its K tiles split: slot 0 the even ceil
+    half, slot 1 the odd floor half), every other group one item of two Q tiles,
+    each exactly once; chunks of slices in order; inside a chunk by K tiles
+    per pipeline: the two-tile items heavier than the heaviest split-Q item
+    (half of its K tiles, rounded up), then the split-Q items, heaviest Q tile
+    first, then the other two-tile items, heaviest group first."""
     lib = ncz.flash.lib()
+    n_groups = math.ceil(s / 256)
     n_qt = math.ceil(s / 128)
-    n_kv = math.ceil(s / 128)
-    items = n_qt * bh
+    low = n_groups - groups
+    split_qt = n_qt - 2 * low
+    items = bh * (split_qt + low)
     chunk = min(chunk, bh)
+    top_half = (k_tiles((n_qt - 1) * 128, s, causal) + 1) // 2  # heaviest split-Q item, per pipeline
     seen = set()
-    prev_chunk, prev_qt = -1, None
+    prev_chunk, prev_key = -1, None
     for i in range(items):
-        sl, q_base, n0, n1, nmax, kstride = qsplit_work(lib, bh, s, causal, chunk, i)
-        assert kstride == 2 and q_base % 128 == 0 and 0 <= q_base < s and 0 <= sl < bh
-        key = (sl, q_base)
+        sl, q_base, n0, n1, nmax, kstride = qsplit_work(lib, bh, s, causal, chunk, groups, i)
+        assert 0 <= sl < bh and 0 <= q_base < s
+        c = sl // chunk
+        assert c >= prev_chunk
+        if kstride == 2:
+            assert q_base % 128 == 0 and q_base // 128 >= 2 * low
+            key = (sl, q_base, "q")
+            total = k_tiles(q_base, s, causal)
+            assert nmax == total and n0 == (total + 1) // 2 and n1 == total // 2
+            order = (1, -q_base)  # heaviest Q tile first
+        else:
+            assert kstride == 1 and q_base % 256 == 0 and q_base // 256 < low
+            key = (sl, q_base, "g")
+            assert (n0, n1) == (k_tiles(q_base, s, causal), k_tiles(q_base + 128, s, causal))
+            assert nmax == max(n0, n1)
+            order = (0 if nmax > top_half else 2, -q_base)
         assert key not in seen
         seen.add(key)
-        c, qt = sl // chunk, q_base // 128
-        assert c >= prev_chunk
         if c == prev_chunk:
-            assert qt <= prev_qt
-        prev_chunk, prev_qt = c, qt
-        total = (min(q_base + 128, s) - 1) // 128 + 1 if causal else n_kv
-        assert nmax == total and n0 == (total + 1) // 2 and n1 == total // 2
+            assert order >= prev_key
+        prev_chunk, prev_key = c, order
     assert len(seen) == items
     out = (ctypes.c_int32 * 6)()
-    assert lib.ncz_test_qsplit_work(bh, s, int(causal), chunk, items, out) != 0
+    assert lib.ncz_test_qsplit_work(bh, s, int(causal), chunk, groups, items, out) != 0
+    assert lib.ncz_test_qsplit_work(bh, s, int(causal), chunk, n_groups + 1, 0, out) != 0
+
+
+@pytest.mark.parametrize("bh,s,sms,groups", [
+    (8, 1024, 148, 4),       # config 2: 32 items, all split
+    (5, 8192, 148, 32),      # 160 items < 1.25 per SM: all split
+    (8, 8192, 148, 0),       # config 4's 8-GPU shard: 256 items
+    (6, 8192, 148, 0),       # 192 items
+    (16, 8192, 148, 0),      # 4-GPU shard
+    (64, 8192, 148, 0),      # config 4 on one GPU
+    (128, 2048, 148, 0),
+    (184, 256, 148, 1),      # 184 one-group items < 185
+    (185, 256, 148, 0),      # 185 = 1.25 * 148
+    (4, 1024, 148, 4),
+])
+def test_split_q_plan(ncz, bh, s, sms, groups):
+    """Every group split-Q when the items of two Q tiles number fewer than
+    1.25 per SM, else none (causal masking or not)."""
+    out = (ctypes.c_int32 * 2)()
+    assert ncz.flash.lib().ncz_test_qsplit_plan(bh, s, sms, out) == 0
+    assert out[0] == groups
+    n_groups, n_qt = math.ceil(s / 256), math.ceil(s / 128)
+    low = n_groups - groups
+    assert out[1] == (bh * (n_qt - 2 * low + low) if groups else bh * n_groups)
 
 
 def test_split_q_mode_hook(ncz):
@@ -112,3 +160,6 @@ def test_split_q_mode_hook(ncz):
     assert lib.ncz_test_set_qsplit(3) != 0 and lib.ncz_test_set_qsplit(-1) != 0
     for mode in (1, 2, 0):
         assert lib.ncz_test_set_qsplit(mode) == 0
+    assert lib.ncz_test_set_qsplit_groups(-2) != 0
+    for groups in (0, 7, 1 << 20, -1):
+        assert lib.ncz_test_set_qsplit_groups(groups) == 0

@@ -54,6 +54,11 @@ QSPLIT_CASES = [  # split-Q items forced in both libraries
     (64, 2048, 64, True, "tma", torch.float16, 0),    # 1024 items of one Q tile
     (300, 600, 32, False, "lsu", torch.float16, 0),   # 1500 items, plain-load producer
 ]
+MIXED_CASES = [  # (case, split-Q groups forced in both libraries)
+    ((10, 4096, 64, True, "tma", torch.float16, 1), 3),     # top 3 of 16 groups split: 190 items
+    ((8, 8192, 64, True, "tma", torch.float16, 1), 4),      # two-tile items before and after the split-Q ones
+    ((6, 2000, 32, False, "lsu", torch.float16, 1), 2),     # ragged S, plain-load producer
+]
 
 
 @pytest.mark.parametrize("case", QSPLIT_CASES, ids=lambda c: f"qsplit_bh{c[0]}_s{c[1]}_d{c[2]}_{c[4]}")
@@ -99,3 +104,17 @@ def check_items(ncz, debug_lib, case):
         assert int(visits[n:].abs().sum()) == 0
         assert ncz.sync_status() == 0
         assert torch.equal(o, want)
+
+
+@pytest.mark.parametrize("case,groups", MIXED_CASES, ids=["bh10_s4096_g3", "bh8_s8192_g4", "bh6_s2000_g2_lsu"])
+def test_mixed_items_started_exactly_once(ncz, debug_lib, case, groups):
+    """A launch whose top groups run as split-Q items and the others as items
+    of two Q tiles, in one item order: every item started once, O identical to
+    the product library's."""
+    lib = ncz.flash.lib()
+    debug_lib.ncz_test_set_qsplit_groups.argtypes = [ctypes.c_int]
+    assert lib.ncz_test_set_qsplit_groups(groups) == 0 and debug_lib.ncz_test_set_qsplit_groups(groups) == 0
+    try:
+        check_items(ncz, debug_lib, case)
+    finally:
+        assert lib.ncz_test_set_qsplit_groups(-1) == 0 and debug_lib.ncz_test_set_qsplit_groups(-1) == 0
