@@ -284,6 +284,19 @@ int ncz_test_set_qsplit(int mode);
  * timing sweeps use it to run one shape under every mix of item kinds. */
 int ncz_test_set_qsplit_groups(int groups);
 
+/* Twin items: a launch with seq_len <= 128 (one Q tile per slice) and no
+ * split-KV runs items of two slices, one per pipeline, unless a test forces
+ * split-Q items.  enable = 1 (the default) allows them, 0 runs items of one
+ * slice; results are bit-identical either way. */
+int ncz_test_set_twin(int enable);
+
+/* Test hook: twin item `item` of a launch of batch_heads slices of seq_len <=
+ * 128: out[0], out[1] = the slices of slots 0 and 1 (-1 when slot 1 is empty),
+ * out[2], out[3] = their K tiles, out[4] = ring tiles of the item, out[5],
+ * out[6] = the slices of ring tiles 0 and 1 (-1 when absent), out[7] = the
+ * item kind (2 = twin).  Host only. */
+int ncz_test_twin_work(size_t batch_heads, size_t seq_len, uint32_t causal, int item, int32_t *out);
+
 /* Bound of every in-kernel mbarrier wait on `device` (-1 = current), in SM
  * cycles; 0 restores the default (4e9, about 2 s).  A test shortens it so an
  * expired wait is seen quickly. */

@@ -73,6 +73,9 @@ std::atomic<int> g_qsplit_mode{0};
 // >= 0: that many split-Q groups (clamped) instead of the mode's choice
 // (ncz_test_set_qsplit_groups); -1 = the mode decides.
 std::atomic<int> g_qsplit_force{-1};
+// Twin items (two slices of one Q tile per item) for launches with
+// seq_len <= 128: 1 = when eligible (default), 0 = never (ncz_test_set_twin).
+std::atomic<int> g_twin_mode{1};
 bool g_init_done = false;
 int g_init_status = NCZ_ERROR_NOT_INITIALIZED;
 std::atomic<uint64_t> g_launches{0};
@@ -425,7 +428,10 @@ int launch_on_current(const Resolved &r, int dev) {
     // Split-Q items (launches without split-KV only): for every group when the
     // items of two Q tiles leave SMs idle, else for the causal groups whose
     // items are longer than an even share of the work (qsplit_plan).
+    // Twin items instead for one Q tile per slice (seq_len <= 128): both
+    // pipelines busy, half the items (unless a test forces split-Q items).
     p.qsplit_groups = 0;
+    p.twin = 0;
     if (p.num_splits == 1) {
         const int mode = g_qsplit_mode.load(std::memory_order_relaxed);
         const int force = g_qsplit_force.load(std::memory_order_relaxed);
@@ -433,14 +439,18 @@ int launch_on_current(const Resolved &r, int dev) {
             p.qsplit_groups = std::min(force, p.num_groups);
         else if (mode == 1)
             p.qsplit_groups = p.num_groups;
+        else if (r.seq <= static_cast<size_t>(ncz::kBlockM) && g_twin_mode.load(std::memory_order_relaxed) != 0)
+            p.twin = 1;
         else if (mode == 0)
             p.qsplit_groups = qsplit_plan(r.bh, r.seq, static_cast<size_t>(device_sms(dev)));
     }
     // One CTA per work item, heaviest first; at most one is resident per SM (TMEM
     // holds one CTA's 512 columns) and it takes over the items of CTAs that have
     // not started yet.
-    const size_t items = p.qsplit_groups > 0 ? qsplit_items(r.bh, r.seq, p.qsplit_groups)
-                                             : static_cast<size_t>(p.num_groups) * r.bh * static_cast<size_t>(p.num_splits);
+    const size_t items = p.twin ? (r.bh + 1) / 2
+                         : p.qsplit_groups > 0
+                             ? qsplit_items(r.bh, r.seq, p.qsplit_groups)
+                             : static_cast<size_t>(p.num_groups) * r.bh * static_cast<size_t>(p.num_splits);
     const unsigned grid = static_cast<unsigned>(items);
 #ifdef NCZ_DEBUG_ITEM_VISITS
     p.item_visits = r.item_visits;
@@ -986,6 +996,38 @@ int ncz_test_item_work(size_t batch_heads, size_t seq_len, uint32_t causal, int 
 int ncz_test_set_qsplit(int mode) {
     if (mode < 0 || mode > 2) return NCZ_ERROR_INVALID_VALUE;
     g_qsplit_mode.store(mode, std::memory_order_relaxed);
+    return NCZ_SUCCESS;
+}
+
+int ncz_test_set_twin(int enable) {
+    if (enable != 0 && enable != 1) return NCZ_ERROR_INVALID_VALUE;
+    g_twin_mode.store(enable, std::memory_order_relaxed);
+    return NCZ_SUCCESS;
+}
+
+int ncz_test_twin_work(size_t batch_heads, size_t seq_len, uint32_t causal, int item, int32_t *out) {
+    if (out == nullptr || batch_heads == 0 || seq_len == 0 || seq_len > static_cast<size_t>(ncz::kBlockM) ||
+        item < 0 || batch_heads > (size_t(1) << 20))
+        return NCZ_ERROR_INVALID_VALUE;
+    if (static_cast<size_t>(item) >= (batch_heads + 1) / 2) return NCZ_ERROR_INVALID_VALUE;
+    FlashParams p{};
+    p.batch_heads = static_cast<int>(batch_heads);
+    p.seq_len = static_cast<int>(seq_len);
+    p.causal = causal != 0;
+    p.num_groups = 1;
+    p.num_splits = 1;
+    p.kv_per_split = 1;
+    p.chunk_slices = 1;
+    p.twin = 1;
+    const ncz::Work wk = ncz::make_work(p, item);
+    out[0] = ncz::slot_slice(wk, 0);
+    out[1] = wk.n[1] > 0 ? ncz::slot_slice(wk, 1) : -1;
+    out[2] = wk.n[0];
+    out[3] = wk.n[1];
+    out[4] = wk.n_max;
+    out[5] = ncz::ring_slice(wk, 0);
+    out[6] = wk.n_max > 1 ? ncz::ring_slice(wk, 1) : -1;
+    out[7] = wk.kind;
     return NCZ_SUCCESS;
 }
 

@@ -155,6 +155,9 @@ struct FlashParams {
     // causal masking; all groups when it equals num_groups) run as split-Q
     // items, the other groups as items of two Q tiles.  0 = none.
     int qsplit_groups;
+    // seq_len <= 128 (one Q tile per slice), no split-KV, no split-Q: twin
+    // items of two slices each, one per pipeline.  0 = items of one slice.
+    int twin;
     float *part_o;
     float *part_ml;
 #ifdef NCZ_DEBUG_ITEM_VISITS
@@ -223,11 +226,17 @@ struct SmemLayout {
 };
 
 // An item as seen by its two pipeline slots p = 0, 1 (pipeline w takes slot
-// w ^ (item count & 1)).  Normally slot p is Q tile p of the item (rows
-// q_base + 128 p ..), visiting K tiles kv0, kv0 + 1, ...; in a split-Q item
-// both slots share Q tile 0 and slot p visits K tiles p, p + 2, p + 4, ...
-// (kstride 2).  Either way slot p's j-th K tile is ring tile j * kstride + p *
+// w ^ (item count & 1)), in one of three kinds:
+// - kPairItem: slot p is Q tile p of the item (rows q_base + 128 p ..),
+//   visiting K tiles kv0, kv0 + 1, ...;
+// - kSplitQItem: both slots share Q tile 0 (rows q_base ..) and slot p visits
+//   K tiles p, p + 2, p + 4, ... (kstride 2);
+// - kTwinItem (slices of one Q tile, seq_len <= 128): slot p is slice
+//   slice + p in Q tile p, visiting its own K tiles 0, 1, ...; the item's ring
+//   tiles alternate between the two slices (kstride 2).
+// In every kind slot p's j-th K tile is ring tile j * kstride + p *
 // (kstride - 1) of the item, and the item streams n_max ring tiles in order.
+constexpr int kPairItem = 0, kSplitQItem = 1, kTwinItem = 2;
 struct Work {
     int slice;
     int q_base;
@@ -236,15 +245,39 @@ struct Work {
     int n[kQTiles];     // K/V tiles slot p visits (0 = none)
     int diag[kQTiles];  // last K tile slot p's rows see at all (the only one with masked keys)
     int n_max;          // K/V ring tiles of the item
-    int kstride;        // 1, or 2 for a split-Q item
+    int kstride;        // 1, or 2 for a split-Q or twin item
+    int kind;
 };
 
-__host__ __device__ __forceinline__ int slot_qtile(const Work &wk, int slot) { return wk.kstride == 2 ? 0 : slot; }
+// Shared-memory Q tile of slot p.
+__host__ __device__ __forceinline__ int slot_qtile(const Work &wk, int slot) {
+    return wk.kind == kSplitQItem ? 0 : slot;
+}
 // Q tile `tile` (0 or 1) of the item is loaded: some slot reads it.
 __host__ __device__ __forceinline__ bool q_tile_used(const Work &wk, int tile) {
-    return wk.kstride == 2 ? (tile == 0 && wk.n[0] > 0) : wk.n[tile] > 0;
+    return wk.kind == kSplitQItem ? (tile == 0 && wk.n[0] > 0) : wk.n[tile] > 0;
 }
 __host__ __device__ __forceinline__ int slot_koff(const Work &wk, int slot) { return wk.kstride == 2 ? slot : 0; }
+// Slice of slot p's rows, and their first row in it.
+__host__ __device__ __forceinline__ int slot_slice(const Work &wk, int slot) {
+    return wk.kind == kTwinItem ? wk.slice + slot : wk.slice;
+}
+__host__ __device__ __forceinline__ int slot_row0(const Work &wk, int slot) {
+    return wk.kind == kPairItem ? wk.q_base + slot * kBlockM : wk.q_base;
+}
+// Index in the sequence of slot p's first K tile, and the step between its K
+// tiles (for masking).
+__host__ __device__ __forceinline__ int slot_seq0(const Work &wk, int slot) {
+    return wk.kind == kSplitQItem ? wk.kv0 + slot : wk.kv0;
+}
+__host__ __device__ __forceinline__ int slot_seq_step(const Work &wk) { return wk.kind == kSplitQItem ? 2 : 1; }
+// Slice and sequence index of ring tile r of the item.
+__host__ __device__ __forceinline__ int ring_slice(const Work &wk, int r) {
+    return wk.kind == kTwinItem ? wk.slice + (r & 1) : wk.slice;
+}
+__host__ __device__ __forceinline__ int ring_seq(const Work &wk, int r) {
+    return wk.kind == kTwinItem ? r >> 1 : wk.kv0 + r;
+}
 
 __device__ uint32_t g_ncz_status = 0u;
 // Bound of every mbarrier wait, in SM cycles (tests shorten it, ncz_test_set_wait_limit).
@@ -260,6 +293,24 @@ __host__ __device__ constexpr int imin(int a, int b) { return a < b ? a : b; }
 __host__ __device__ __forceinline__ Work make_work(const FlashParams &p, int item) {
     Work wk;
     const int n_kv = (p.seq_len + kBlockN - 1) / kBlockN;
+    if (p.twin) {
+        // Item i: slices 2i and 2i + 1 (the last item of an odd count has slot
+        // 1 empty), each one Q tile against all of its K tiles (its only one
+        // holding masked keys under causal masking: seq_len <= 128).
+        wk.slice = 2 * item;
+        wk.q_base = 0;
+        wk.split = 0;
+        wk.kv0 = 0;
+        wk.kstride = 2;
+        wk.kind = kTwinItem;
+        const int last_row = p.seq_len - 1;
+        const int total = p.causal ? last_row / kBlockN + 1 : n_kv;
+        wk.n[0] = total;
+        wk.n[1] = 2 * item + 1 < p.batch_heads ? total : 0;
+        wk.diag[0] = wk.diag[1] = total - 1;
+        wk.n_max = wk.n[1] > 0 ? 2 * total : 2 * total - 1;
+        return wk;
+    }
     if (p.qsplit_groups > 0) {
         // Chunks of chunk_slices slices; inside a chunk the items by K tiles
         // per pipeline, heaviest first: the items of two Q tiles that visit
@@ -294,6 +345,7 @@ __host__ __device__ __forceinline__ Work make_work(const FlashParams &p, int ite
             wk.diag[0] = wk.diag[1] = total - 1;
             wk.n_max = total;
             wk.kstride = 2;
+            wk.kind = kSplitQItem;
             return wk;
         }
         const int rem = off < slices * lead ? off : off - slices * split_qt;  // place among the two-tile items
@@ -302,6 +354,7 @@ __host__ __device__ __forceinline__ Work make_work(const FlashParams &p, int ite
         wk.q_base = group * (kQTiles * kBlockM);
         wk.n_max = 0;
         wk.kstride = 1;
+        wk.kind = kPairItem;
 #pragma unroll
         for (int w = 0; w < kQTiles; ++w) {
             const int q0 = wk.q_base + w * kBlockM;
@@ -330,6 +383,7 @@ __host__ __device__ __forceinline__ Work make_work(const FlashParams &p, int ite
     wk.kv0 = wk.split * p.kv_per_split;
     wk.n_max = 0;
     wk.kstride = 1;
+    wk.kind = kPairItem;
 #pragma unroll
     for (int w = 0; w < kQTiles; ++w) {
         const int q0 = wk.q_base + w * kBlockM;
@@ -468,7 +522,7 @@ __device__ __forceinline__ void producer_tma(const FlashParams &p, const CUtenso
         for (int w = 0; w < kQTiles; ++w)
             if (q_tile_used(wk, w))
                 tma_load_3d_elect(sbase + L::kOffQ + qs * L::kQSlot + w * L::kQTile, tq, b.q_full(qs), 0,
-                                  wk.q_base + w * kBlockM, wk.slice);
+                                  slot_row0(wk, w), slot_slice(wk, w));
         const int cur = it++;
         const bool walk = wk.n_max < p.walk_tiles;
         const int req_at = wk.n_max > kClcLead ? wk.n_max - kClcLead : 0;  // see kClcLead
@@ -486,11 +540,11 @@ __device__ __forceinline__ void producer_tma(const FlashParams &p, const CUtenso
                 pending = cur;
             }
             mbar_arrive_expect_tx_elect(b.k_full(st), L::kKvTile);
-            tma_load_3d_elect(sbase + L::kOffK + st * L::kKvTile, tk, b.k_full(st), 0, (wk.kv0 + j) * kBlockN,
-                              wk.slice);
+            tma_load_3d_elect(sbase + L::kOffK + st * L::kKvTile, tk, b.k_full(st), 0, ring_seq(wk, j) * kBlockN,
+                              ring_slice(wk, j));
             mbar_arrive_expect_tx_elect(b.v_full(st), L::kKvTile);
-            tma_load_3d_elect(sbase + L::kOffV + st * L::kKvTile, tv, b.v_full(st), 0, (wk.kv0 + j) * kBlockN,
-                              wk.slice);
+            tma_load_3d_elect(sbase + L::kOffV + st * L::kKvTile, tv, b.v_full(st), 0, ring_seq(wk, j) * kBlockN,
+                              ring_slice(wk, j));
         }
         if (!ok) break;
         if (walk && wk.n_max == 0) {  // no K tiles: ask now
@@ -553,9 +607,6 @@ __device__ __forceinline__ void producer_lsu(const FlashParams &p, uint8_t *smem
     for (int item = static_cast<int>(blockIdx.x); ok && item >= 0;) {
         const Work wk = make_work(p, item);
         count_item_visit(p, item, lane);
-        const uint16_t *qs = p.q + wk.slice * p.q_stride;
-        const uint16_t *ks = p.k + wk.slice * p.k_stride;
-        const uint16_t *vs = p.v + wk.slice * p.v_stride;
         const int slot = it & 1;
         if (it >= 2 && !warp_wait(b.q_empty(slot), ((it >> 1) - 1) & 1, abort_flag, kSiteQEmpty)) break;
         const int cur = it++;
@@ -564,8 +615,9 @@ __device__ __forceinline__ void producer_lsu(const FlashParams &p, uint8_t *smem
 #pragma unroll
         for (int w = 0; w < kQTiles; ++w)
             if (q_tile_used(wk, w))
-                lsu_tile<D, kBlockM>(smem + L::kOffQ + slot * L::kQSlot + w * L::kQTile, qs, p.q_row,
-                                     wk.q_base + w * kBlockM, p.seq_len, lane);
+                lsu_tile<D, kBlockM>(smem + L::kOffQ + slot * L::kQSlot + w * L::kQTile,
+                                     p.q + slot_slice(wk, w) * p.q_stride, p.q_row, slot_row0(wk, w), p.seq_len,
+                                     lane);
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(b.q_full(slot));
@@ -582,13 +634,13 @@ __device__ __forceinline__ void producer_lsu(const FlashParams &p, uint8_t *smem
                 }
                 pending = cur;
             }
-            lsu_tile<D, kBlockN>(smem + L::kOffK + st * L::kKvTile, ks, p.k_row, (wk.kv0 + j) * kBlockN, p.seq_len,
-                                 lane);
+            lsu_tile<D, kBlockN>(smem + L::kOffK + st * L::kKvTile, p.k + ring_slice(wk, j) * p.k_stride, p.k_row,
+                                 ring_seq(wk, j) * kBlockN, p.seq_len, lane);
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(b.k_full(st));
-            lsu_tile<D, kBlockN>(smem + L::kOffV + st * L::kKvTile, vs, p.v_row, (wk.kv0 + j) * kBlockN, p.seq_len,
-                                 lane);
+            lsu_tile<D, kBlockN>(smem + L::kOffV + st * L::kKvTile, p.v + ring_slice(wk, j) * p.v_stride, p.v_row,
+                                 ring_seq(wk, j) * kBlockN, p.seq_len, lane);
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(b.v_full(st));
@@ -780,10 +832,10 @@ __device__ __forceinline__ void store_cols(uint32_t taddr, const float (&o)[N]) 
 // Writes O[row][0 .. N) = o / l (f32 or f16, vector stores when aligned), as
 // o * (1 / l): one division per row instead of N.
 template <int N>
-__device__ __forceinline__ void write_o_global(const FlashParams &p, const Work &wk, int row, const float (&o)[N],
+__device__ __forceinline__ void write_o_global(const FlashParams &p, int slice, int row, const float (&o)[N],
                                                float l) {
     const float inv = 1.0f / l;
-    const long long base = wk.slice * p.o_stride + static_cast<long long>(row) * p.o_row;
+    const long long base = static_cast<long long>(slice) * p.o_stride + static_cast<long long>(row) * p.o_row;
     if (p.o_dtype != 0) {  // 16-bit O: f16 (1) or bf16 (2)
         uint16_t *orow = reinterpret_cast<uint16_t *>(p.o) + base;
         const bool bf = p.o_dtype == 2;
@@ -994,9 +1046,9 @@ __device__ __forceinline__ void softmax_role(const FlashParams &p, uint8_t *smem
             walk = wk.n_max < p.walk_tiles;
             const int wq = w ^ (it & 1);  // slot of the item this pipeline takes
             n = wq ? wk.n[1] : wk.n[0];
-            row = wk.q_base + slot_qtile(wk, wq) * kBlockM + r;
-            ks = wk.kstride;
-            kv0 = wk.kv0 + slot_koff(wk, wq);  // the slot's j-th K tile is kv0 + j * ks
+            row = slot_row0(wk, wq) + r;
+            ks = slot_seq_step(wk);
+            kv0 = slot_seq0(wk, wq);  // the slot's j-th K tile is kv0 + j * ks in its sequence
             diag = wq ? wk.diag[1] : wk.diag[0];
         }
         if (n == 0) {  // no rows of this pipeline in the item: nothing staged in its Q tile
@@ -1106,7 +1158,7 @@ __device__ __forceinline__ void softmax_role(const FlashParams &p, uint8_t *smem
         it = stash[1];
         const Work wk = make_work(p, item);
         const int wq = w ^ (it & 1);
-        const bool qsp = wk.kstride == 2;
+        const bool qsp = wk.kind == kSplitQItem;
         // A split-Q item whose both slots visited K tiles: slot 0's warp writes the
         // rows, merging slot 1's state (same TMEM lanes, the other pipeline's
         // columns) into its own: O = (2^(m0-M) O0 + 2^(m1-M) O1) /
@@ -1165,15 +1217,15 @@ __device__ __forceinline__ void softmax_role(const FlashParams &p, uint8_t *smem
         // has arrived on q_empty.
         const int stile = qsp ? 1 : wq;
         uint8_t *stage = smem + L::kOffQ + (it & 1) * L::kQSlot + stile * L::kQTile + sub * 32 * L::kSpan;
-        const int row0 = wk.q_base + slot_qtile(wk, wq) * kBlockM + sub * 32;  // this warp's first row
+        const int row0 = slot_row0(wk, wq) + sub * 32;  // this warp's first row
         const int valid = imin(32, seq_len - row0);
         if (p.num_splits > 1) {
             write_partial_staged<D>(p, wk, row0, row, o, m, l, stage, valid, lane);
         } else if (D >= 32 && p.o_vec) {
             // (at d=16 a staging row is 32 bytes: measured 5 % slower than direct stores)
-            write_o_staged<D>(p, wk.slice, row0, o, l, stage, valid, lane);
+            write_o_staged<D>(p, slot_slice(wk, wq), row0, o, l, stage, valid, lane);
         } else if (row < seq_len) {
-            write_o_global<D>(p, wk, row, o, l);
+            write_o_global<D>(p, slot_slice(wk, wq), row, o, l);
         }
         fence_proxy_async_smem();  // the staging accesses precede the slot's next TMA write
         __syncwarp();

@@ -707,3 +707,47 @@ def test_mixed_split_q_and_two_tile_items(ncz, oracle_mod, qsplit_mode):
     C.check(run(ncz, p), want, idx, "automatic plan")
     qsplit_mode(2)
     C.check(run(ncz, p), want, idx, "two-tile items only")
+
+
+TWIN_CASES = [(513, 128, 32, False), (7, 77, 64, True), (2, 1, 16, True), (64, 128, 64, True), (5, 100, 16, False),
+              (1, 128, 64, True)]
+
+
+@pytest.fixture
+def twin_mode(ncz):
+    """Sets the twin-item choice for one test and restores the default."""
+    lib = ncz.flash.lib()
+
+    def set_mode(enable):
+        assert lib.ncz_test_set_twin(enable) == 0
+
+    yield set_mode
+    assert lib.ncz_test_set_twin(1) == 0
+
+
+@pytest.mark.parametrize("case", TWIN_CASES, ids=lambda c: f"bh{c[0]}_s{c[1]}_d{c[2]}_c{int(c[3])}")
+def test_twin_items_match_oracle(ncz, oracle_mod, twin_mode, case):
+    """seq_len <= 128: items of two slices, one per pipeline (odd counts leave
+    the last item's second slot empty), against the oracle; both producers
+    give the same bits, and so do items of one slice."""
+    bh, s, d, causal = case
+    p = C.normal_problem(bh, s, d, causal, 61 + bh, oracle_mod, std=0.7)
+    want = C.reference(p, oracle_mod)
+    idx = C.active_index(p)
+    a = run(ncz, p, producer="tma")
+    assert np.array_equal(a, run(ncz, p, producer="lsu"))
+    C.check(a, want, idx, "twin items")
+    C.check(run(ncz, p, o_dtype="float16"), want, idx, "twin items f16 O", o_unit=2.0 ** -11)
+    twin_mode(0)
+    assert np.array_equal(a, run(ncz, p, producer="tma"))
+
+
+def test_twin_items_bf16(ncz, oracle_mod, twin_mode):
+    """bf16 inputs through twin items, against the oracle; items of one slice
+    give the same bits."""
+    pb = C.normal_problem_bf16(9, 100, 32, True, 71, oracle_mod, std=0.7)
+    got = _run_bf16(ncz, pb)
+    C.check(got, C.reference(pb, oracle_mod), C.active_index(pb), "twin bf16", atol=C.ATOL_BF16,
+            p_unit=C.P_UNIT_BF16)
+    twin_mode(0)
+    assert np.array_equal(got, _run_bf16(ncz, pb))

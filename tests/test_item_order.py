@@ -163,3 +163,35 @@ def test_split_q_mode_hook(ncz):
     assert lib.ncz_test_set_qsplit_groups(-2) != 0
     for groups in (0, 7, 1 << 20, -1):
         assert lib.ncz_test_set_qsplit_groups(groups) == 0
+
+
+@pytest.mark.parametrize("bh", [1, 2, 5, 512, 513])
+@pytest.mark.parametrize("s,causal", [(1, True), (77, False), (128, True), (128, False)])
+def test_twin_item_order(ncz, bh, s, causal):
+    """Twin items (seq_len <= 128): item i holds slices 2i and 2i + 1, one per
+    slot, each against its one K tile; ring tile r is slice 2i + r's tile; the
+    last item of an odd count has slot 1 empty and one ring tile."""
+    lib = ncz.flash.lib()
+    out = (ctypes.c_int32 * 8)()
+    items = (bh + 1) // 2
+    seen = []
+    for i in range(items):
+        assert lib.ncz_test_twin_work(bh, s, int(causal), i, out) == 0
+        s0, s1, n0, n1, n_max, r0, r1, kind = list(out)
+        assert kind == 2 and s0 == 2 * i and n0 == 1 and r0 == s0
+        if 2 * i + 1 < bh:
+            assert (s1, n1, n_max, r1) == (2 * i + 1, 1, 2, 2 * i + 1)
+            seen += [s0, s1]
+        else:
+            assert (s1, n1, n_max, r1) == (-1, 0, 1, -1)
+            seen.append(s0)
+    assert seen == list(range(bh))
+    assert lib.ncz_test_twin_work(bh, s, int(causal), items, out) != 0
+    assert lib.ncz_test_twin_work(bh, 129, int(causal), 0, out) != 0
+
+
+def test_twin_hook(ncz):
+    lib = ncz.flash.lib()
+    assert lib.ncz_test_set_twin(2) != 0 and lib.ncz_test_set_twin(-1) != 0
+    for v in (0, 1):
+        assert lib.ncz_test_set_twin(v) == 0

@@ -29,6 +29,8 @@ CASES = [  # (bh, S, d, causal, producer, in_dtype, splits)
     (1, 8192, 64, True, "tma", torch.float16, 0),     # split-KV with empty ranges
     (37, 1000, 16, True, "lsu", torch.float16, 0),    # plain-load producer
     (20, 4096, 64, True, "tma", torch.bfloat16, 3),   # bf16 inputs, explicit split
+    (513, 128, 32, False, "tma", torch.float16, 0),   # twin items, odd slice count
+    (9, 100, 64, True, "lsu", torch.bfloat16, 0),     # twin items, plain-load producer
 ]
 
 
