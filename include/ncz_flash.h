@@ -290,11 +290,16 @@ int ncz_test_set_qsplit_groups(int groups);
  * slice; results are bit-identical either way. */
 int ncz_test_set_twin(int enable);
 
+/* Test hook: out[0] = rows per Q tile (128), out[1] = keys per K/V tile (64):
+ * the units of the item-order and split-plan hooks' tile counts. */
+int ncz_test_tile_shape(int32_t *out);
+
 /* Test hook: twin item `item` of a launch of batch_heads slices of seq_len <=
  * 128: out[0], out[1] = the slices of slots 0 and 1 (-1 when slot 1 is empty),
  * out[2], out[3] = their K tiles, out[4] = ring tiles of the item, out[5],
  * out[6] = the slices of ring tiles 0 and 1 (-1 when absent), out[7] = the
- * item kind (2 = twin).  Host only. */
+ * item kind (2 = twin; 0 = one slice, the last item of an odd count).  Host
+ * only. */
 int ncz_test_twin_work(size_t batch_heads, size_t seq_len, uint32_t causal, int item, int32_t *out);
 
 /* Bound of every in-kernel mbarrier wait on `device` (-1 = current), in SM

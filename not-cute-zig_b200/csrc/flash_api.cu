@@ -305,9 +305,10 @@ int device_sms(int dev) {
 }
 
 // Split-KV ranges for a launch.  Automatic: only when the grid fills at most
-// half the SMs and the K range is long (>= 16 tiles; each range keeps >= 4).  A
-// CTA costs about the time of 4-5 K tiles in fixed set-up and hand-off, and the
-// merge is a second launch, so shorter ranges (config 2: 8 tiles) gain nothing.
+// half the SMs and the K range is long (>= 2048 keys; each range keeps >= 512).
+// A CTA costs about the time of 512-640 keys in fixed set-up and hand-off, and
+// the merge is a second launch, so shorter ranges (config 2: 1024 keys) gain
+// nothing.
 // Split-KV ranges for a launch of bh slices of seq rows on `sms` SMs;
 // requested 0 = automatic, 1 = none, n = up to n ranges.
 void split_plan(size_t bh, size_t seq, int requested, size_t sms, int *splits, int *per_split) {
@@ -316,9 +317,10 @@ void split_plan(size_t bh, size_t seq, int requested, size_t sms, int *splits, i
     int want = requested;
     if (want == 0) {
         want = 1;
-        if (ctas * 2 <= sms && n_kv >= 16) {
+        constexpr int kMinTiles = 2048 / ncz::kBlockN, kRangeTiles = 512 / ncz::kBlockN;
+        if (ctas * 2 <= sms && n_kv >= kMinTiles) {
             const int by_sms = static_cast<int>((sms + ctas - 1) / ctas);
-            want = std::min(std::min(by_sms, n_kv / 4), ncz::kMaxSplits);
+            want = std::min(std::min(by_sms, n_kv / kRangeTiles), ncz::kMaxSplits);
         }
     }
     want = std::max(1, std::min(std::min(want, n_kv), ncz::kMaxSplits));
@@ -996,6 +998,13 @@ int ncz_test_item_work(size_t batch_heads, size_t seq_len, uint32_t causal, int 
 int ncz_test_set_qsplit(int mode) {
     if (mode < 0 || mode > 2) return NCZ_ERROR_INVALID_VALUE;
     g_qsplit_mode.store(mode, std::memory_order_relaxed);
+    return NCZ_SUCCESS;
+}
+
+int ncz_test_tile_shape(int32_t *out) {
+    if (out == nullptr) return NCZ_ERROR_INVALID_VALUE;
+    out[0] = ncz::kBlockM;
+    out[1] = ncz::kBlockN;
     return NCZ_SUCCESS;
 }
 

@@ -294,21 +294,29 @@ __host__ __device__ __forceinline__ Work make_work(const FlashParams &p, int ite
     Work wk;
     const int n_kv = (p.seq_len + kBlockN - 1) / kBlockN;
     if (p.twin) {
-        // Item i: slices 2i and 2i + 1 (the last item of an odd count has slot
-        // 1 empty), each one Q tile against all of its K tiles (its only one
-        // holding masked keys under causal masking: seq_len <= 128).
+        // Item i: slices 2i and 2i + 1, each one Q tile against all of its K
+        // tiles (seq_len <= 128).  The last item of an odd count is an item of
+        // one slice (Q tile 0; its Q tile 1 starts past seq_len), so the ring
+        // never names a slice past the last.
         wk.slice = 2 * item;
         wk.q_base = 0;
         wk.split = 0;
         wk.kv0 = 0;
-        wk.kstride = 2;
-        wk.kind = kTwinItem;
         const int last_row = p.seq_len - 1;
         const int total = p.causal ? last_row / kBlockN + 1 : n_kv;
         wk.n[0] = total;
-        wk.n[1] = 2 * item + 1 < p.batch_heads ? total : 0;
         wk.diag[0] = wk.diag[1] = total - 1;
-        wk.n_max = wk.n[1] > 0 ? 2 * total : 2 * total - 1;
+        if (2 * item + 1 < p.batch_heads) {
+            wk.n[1] = total;
+            wk.n_max = 2 * total;
+            wk.kstride = 2;
+            wk.kind = kTwinItem;
+        } else {
+            wk.n[1] = 0;
+            wk.n_max = total;
+            wk.kstride = 1;
+            wk.kind = kPairItem;
+        }
         return wk;
     }
     if (p.qsplit_groups > 0) {

@@ -123,6 +123,7 @@ _SIGNATURES = {
     "ncz_test_set_qsplit": (ctypes.c_int, [ctypes.c_int]),
     "ncz_test_set_qsplit_groups": (ctypes.c_int, [ctypes.c_int]),
     "ncz_test_set_twin": (ctypes.c_int, [ctypes.c_int]),
+    "ncz_test_tile_shape": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int32)]),
     "ncz_test_twin_work": (ctypes.c_int, [_SZ, _SZ, ctypes.c_uint32, ctypes.c_int, ctypes.POINTER(ctypes.c_int32)]),
     "ncz_test_qsplit_work": (ctypes.c_int, [_SZ, _SZ, ctypes.c_uint32, ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                             ctypes.POINTER(ctypes.c_int32)]),

@@ -726,10 +726,11 @@ def twin_mode(ncz):
 
 
 @pytest.mark.parametrize("case", TWIN_CASES, ids=lambda c: f"bh{c[0]}_s{c[1]}_d{c[2]}_c{int(c[3])}")
-def test_twin_items_match_oracle(ncz, oracle_mod, twin_mode, case):
-    """seq_len <= 128: items of two slices, one per pipeline (odd counts leave
-    the last item's second slot empty), against the oracle; both producers
-    give the same bits, and so do items of one slice."""
+def test_twin_items_match_oracle(ncz, oracle_mod, twin_mode, qsplit_mode, case):
+    """seq_len <= 128: items of two slices, one per pipeline (an odd count
+    ends with an item of one slice), against the oracle; both producers give
+    the same bits, and so do items of one slice (with split-Q items off too:
+    those merge two states, which rounds differently)."""
     bh, s, d, causal = case
     p = C.normal_problem(bh, s, d, causal, 61 + bh, oracle_mod, std=0.7)
     want = C.reference(p, oracle_mod)
@@ -739,15 +740,18 @@ def test_twin_items_match_oracle(ncz, oracle_mod, twin_mode, case):
     C.check(a, want, idx, "twin items")
     C.check(run(ncz, p, o_dtype="float16"), want, idx, "twin items f16 O", o_unit=2.0 ** -11)
     twin_mode(0)
+    C.check(run(ncz, p, producer="tma"), want, idx, "twin off (automatic plan)")
+    qsplit_mode(2)
     assert np.array_equal(a, run(ncz, p, producer="tma"))
 
 
-def test_twin_items_bf16(ncz, oracle_mod, twin_mode):
+def test_twin_items_bf16(ncz, oracle_mod, twin_mode, qsplit_mode):
     """bf16 inputs through twin items, against the oracle; items of one slice
-    give the same bits."""
+    (split-Q items off) give the same bits."""
     pb = C.normal_problem_bf16(9, 100, 32, True, 71, oracle_mod, std=0.7)
     got = _run_bf16(ncz, pb)
     C.check(got, C.reference(pb, oracle_mod), C.active_index(pb), "twin bf16", atol=C.ATOL_BF16,
             p_unit=C.P_UNIT_BF16)
     twin_mode(0)
+    qsplit_mode(2)
     assert np.array_equal(got, _run_bf16(ncz, pb))

@@ -6,6 +6,12 @@ import math
 import pytest
 
 
+def key_tile(lib):
+    out = (ctypes.c_int32 * 2)()
+    assert lib.ncz_test_tile_shape(out) == 0
+    return out[1]
+
+
 def split_plan(lib, bh, seq, requested, sms=148):
     out = (ctypes.c_int32 * 2)()
     assert lib.ncz_test_split_plan(bh, seq, requested, sms, out) == 0
@@ -16,14 +22,15 @@ def split_plan(lib, bh, seq, requested, sms=148):
                                     (64, 8192), (37, 5000), (100, 16384)])
 def test_automatic_split_policy(ncz, bh, seq):
     """Split only when the grid fills at most half the SMs and the K range has
-    at least 16 tiles; at most 8 ranges of at least 4 tiles; ranges cover all
+    at least 2048 keys; at most 8 ranges of at least 512 keys; ranges cover all
     K tiles."""
     lib = ncz.flash.lib()
-    n_kv = math.ceil(seq / 128)
+    kt = key_tile(lib)
+    n_kv = math.ceil(seq / kt)
     items = math.ceil(seq / 256) * bh
     splits, per = split_plan(lib, bh, seq, 0)
-    if items * 2 <= 148 and n_kv >= 16:
-        assert splits > 1 and per >= 4 and splits <= 8
+    if items * 2 <= 148 and n_kv >= 2048 // kt:
+        assert splits > 1 and per >= 512 // kt and splits <= 8
         assert splits <= math.ceil(148 / items)
     else:
         assert splits == 1 and per == n_kv
@@ -34,7 +41,7 @@ def test_automatic_split_policy(ncz, bh, seq):
 @pytest.mark.parametrize("seq", [128, 1000, 4096])
 def test_requested_splits(ncz, requested, seq):
     lib = ncz.flash.lib()
-    n_kv = math.ceil(seq / 128)
+    n_kv = math.ceil(seq / key_tile(lib))
     splits, per = split_plan(lib, 3, seq, requested)
     assert splits <= min(requested, n_kv, 8)
     assert per == math.ceil(n_kv / min(requested, n_kv, 8))

@@ -9,6 +9,13 @@ import math
 import pytest
 
 
+def key_tile(lib):
+    """Keys per K/V tile of the kernel (the unit of the hooks' tile counts)."""
+    out = (ctypes.c_int32 * 2)()
+    assert lib.ncz_test_tile_shape(out) == 0 and out[0] == 128
+    return out[1]
+
+
 def work(lib, bh, s, causal, splits, chunk, i):
     out = (ctypes.c_int32 * 8)()
     assert lib.ncz_test_item_work(bh, s, int(causal), splits, chunk, i, out) == 0
@@ -33,7 +40,8 @@ def check_item_order(lib, bh, s, causal, splits, chunk):
     first inside a chunk, each Q tile's K tiles inside its range and causal
     bound; one item past the end is refused."""
     groups = math.ceil(s / 256)
-    n_kv = math.ceil(s / 128)
+    kt = key_tile(lib)
+    n_kv = math.ceil(s / kt)
     ns = work(lib, bh, s, causal, splits, chunk, 0)[7]
     per = math.ceil(n_kv / min(splits, n_kv))
     assert ns == math.ceil(n_kv / per)
@@ -55,7 +63,7 @@ def check_item_order(lib, bh, s, causal, splits, chunk):
         assert kv0 == sp * per
         for w, n in ((0, n0), (1, n1)):
             q0 = q_base + 128 * w
-            total = 0 if q0 >= s else ((min(q0 + 128, s) - 1) // 128 + 1 if causal else n_kv)
+            total = 0 if q0 >= s else ((min(q0 + 128, s) - 1) // kt + 1 if causal else n_kv)
             assert n == max(0, min(total, kv0 + per) - kv0)
         assert nmax == max(n0, n1)
     assert len(seen) == items
@@ -69,11 +77,11 @@ def qsplit_work(lib, bh, s, causal, chunk, groups, i):
     return list(out)
 
 
-def k_tiles(q_base, s, causal):
-    """K tiles a Q tile starting at q_base visits (reference tile_end)."""
+def k_tiles(q_base, s, causal, kt):
+    """K tiles (of kt keys) a Q tile starting at q_base visits (reference tile_end)."""
     if q_base >= s:
         return 0
-    return (min(q_base + 128, s) - 1) // 128 + 1 if causal else math.ceil(s / 128)
+    return (min(q_base + 128, s) - 1) // kt + 1 if causal else math.ceil(s / kt)
 
 
 @pytest.mark.parametrize("bh,s,causal,chunk,groups", [
@@ -101,7 +109,8 @@ def test_split_q_item_order(ncz, bh, s, causal, chunk, groups):
     split_qt = n_qt - 2 * low
     items = bh * (split_qt + low)
     chunk = min(chunk, bh)
-    top_half = (k_tiles((n_qt - 1) * 128, s, causal) + 1) // 2  # heaviest split-Q item, per pipeline
+    kt = key_tile(lib)
+    top_half = (k_tiles((n_qt - 1) * 128, s, causal, kt) + 1) // 2  # heaviest split-Q item, per pipeline
     seen = set()
     prev_chunk, prev_key = -1, None
     for i in range(items):
@@ -112,13 +121,13 @@ def test_split_q_item_order(ncz, bh, s, causal, chunk, groups):
         if kstride == 2:
             assert q_base % 128 == 0 and q_base // 128 >= 2 * low
             key = (sl, q_base, "q")
-            total = k_tiles(q_base, s, causal)
+            total = k_tiles(q_base, s, causal, kt)
             assert nmax == total and n0 == (total + 1) // 2 and n1 == total // 2
             order = (1, -q_base)  # heaviest Q tile first
         else:
             assert kstride == 1 and q_base % 256 == 0 and q_base // 256 < low
             key = (sl, q_base, "g")
-            assert (n0, n1) == (k_tiles(q_base, s, causal), k_tiles(q_base + 128, s, causal))
+            assert (n0, n1) == (k_tiles(q_base, s, causal, kt), k_tiles(q_base + 128, s, causal, kt))
             assert nmax == max(n0, n1)
             order = (0 if nmax > top_half else 2, -q_base)
         assert key not in seen
@@ -169,21 +178,25 @@ def test_split_q_mode_hook(ncz):
 @pytest.mark.parametrize("s,causal", [(1, True), (77, False), (128, True), (128, False)])
 def test_twin_item_order(ncz, bh, s, causal):
     """Twin items (seq_len <= 128): item i holds slices 2i and 2i + 1, one per
-    slot, each against its one K tile; ring tile r is slice 2i + r's tile; the
-    last item of an odd count has slot 1 empty and one ring tile."""
+    slot, each against all of its K tiles; the ring alternates between the two
+    slices; the last item of an odd count is an item of one slice."""
     lib = ncz.flash.lib()
+    kt = key_tile(lib)
+    total = math.ceil(s / kt)
     out = (ctypes.c_int32 * 8)()
     items = (bh + 1) // 2
     seen = []
     for i in range(items):
         assert lib.ncz_test_twin_work(bh, s, int(causal), i, out) == 0
         s0, s1, n0, n1, n_max, r0, r1, kind = list(out)
-        assert kind == 2 and s0 == 2 * i and n0 == 1 and r0 == s0
+        assert s0 == 2 * i and n0 == total and r0 == s0
         if 2 * i + 1 < bh:
-            assert (s1, n1, n_max, r1) == (2 * i + 1, 1, 2, 2 * i + 1)
+            assert (kind, s1, n1, n_max) == (2, 2 * i + 1, total, 2 * total)
+            assert r1 == 2 * i + 1
             seen += [s0, s1]
         else:
-            assert (s1, n1, n_max, r1) == (-1, 0, 1, -1)
+            assert (kind, s1, n1, n_max) == (0, -1, 0, total)
+            assert r1 == (s0 if total > 1 else -1)
             seen.append(s0)
     assert seen == list(range(bh))
     assert lib.ncz_test_twin_work(bh, s, int(causal), items, out) != 0
