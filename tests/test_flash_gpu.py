@@ -422,23 +422,24 @@ def test_expired_wait_reports_device_timeout_and_context_survives(ncz, oracle_mo
     C.check(got, C.reference(p, oracle_mod), C.active_index(p), "launch after an expired wait")
 
 
-def test_reference_kernel_names(ncz):
+def test_reference_kernel_names(ncz, oracle_mod):
     """launch_named with the reference's kernel names: the same bits as
-    flash.launch for every name that takes the head_dim; h64_causal is causal
-    with the flag off; a head_dim the name does not take leaves O untouched."""
+    flash.launch (itself checked against the oracle) for every name that takes
+    the head_dim; h64_causal is causal with the flag off; a head_dim the name
+    does not take leaves O untouched."""
     dev = torch.device("cuda:0")
-    g = torch.Generator(device=dev)
-    g.manual_seed(11)
 
-    def problem(bh, s, d):
-        q, k, v = (torch.randn(bh * s * d, generator=g, device=dev).half() for _ in range(3))
-        return q, k, v, ncz.Options(seq_len=s, head_dim=d, q_stride=s * d, k_stride=s * d, v_stride=s * d,
-                                    o_stride=s * d, scale=1.0 / math.sqrt(d), batch_heads=bh, causal=True)
+    def problem(bh, s, d, seed):
+        p = C.normal_problem(bh, s, d, True, seed, oracle_mod, std=1.0)
+        q, k, v = (torch.from_numpy(a).to(dev) for a in (p.q, p.k, p.v))
+        return p, q, k, v, ncz.Options(seq_len=s, head_dim=d, q_stride=s * d, k_stride=s * d, v_stride=s * d,
+                                       o_stride=s * d, scale=1.0 / math.sqrt(d), batch_heads=bh, causal=True)
 
     for d in (16, 32, 64):
-        q, k, v, opts = problem(3, 700, d)
+        p, q, k, v, opts = problem(3, 700, d, 11 + d)
         want = torch.zeros(q.numel(), dtype=torch.float32, device=dev)
         ncz.launch(q, k, v, want, opts)
+        C.check(want.cpu().numpy(), C.reference(p, oracle_mod), C.active_index(p), f"flash.launch d={d}")
         for name in ncz.flash.REFERENCE_KERNELS:
             dims, always_causal = ncz.flash.kernel_info(name)
             o = torch.full_like(want, 7.0)
@@ -448,7 +449,7 @@ def test_reference_kernel_names(ncz):
                 assert torch.equal(o, want), (name, d)
             else:
                 assert bool((o == 7.0).all()), (name, d)
-    q, k, v, opts = problem(2, 513, 64)
+    _, q, k, v, opts = problem(2, 513, 64, 91)
     want = torch.zeros(q.numel(), dtype=torch.float32, device=dev)
     ncz.launch(q, k, v, want, opts)
     opts.causal = False

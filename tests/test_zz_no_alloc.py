@@ -8,12 +8,12 @@ not block on an allocation or fail on one mid-request when memory is tight. For
 them the split-KV partials go to a fixed 16 MiB array of the library's device
 image instead of the memory pool of ncz_flash_fwd_splits.
 
-The test runs the new entry point on two and then three calls in a row, with
-different shapes and inputs. The shared array then holds the previous call's
-partials, so stale contents would show. Each output is checked against the
-allocating entry point on the same inputs, within the parity tolerance of the
-other GPU tests. An explicit split count too large for the array must be
-refused with OutOfMemory before any launch.
+The test runs the new entry point on three calls in a row, with different
+shapes and inputs. The shared array then holds the previous call's partials,
+so stale contents would show. Each output is checked against the oracle on the
+same f16 inputs (the parity gate of the other GPU tests) and against the
+allocating entry point. An explicit split count too large for the array must
+be refused with OutOfMemory before any launch.
 
 This file is collected last, so a run that stops at its first failure has
 already run every other test.
@@ -21,6 +21,8 @@ already run every other test.
 import ctypes
 
 import pytest
+
+from tests import cases as C
 
 pytestmark = pytest.mark.gpu
 
@@ -48,13 +50,14 @@ def _desc(ncz, q, k, v, o, bh, s, d, causal):
     return x
 
 
-def test_no_alloc_entry_matches_allocating_entry_on_calls_in_a_row(ncz):
+def test_no_alloc_entry_matches_oracle_on_calls_in_a_row(ncz, oracle_mod):
     lib = ncz.flash.lib()
     # (bh, S, d, causal, seed): each splits its K range, so the scratch is used;
     # the third call repeats the first shape with new inputs.
     calls = [(1, 4096, 64, True, 1), (2, 3000, 32, False, 2), (1, 4096, 64, True, 3)]
     for bh, s, d, causal, seed in calls:
-        q, k, v = _inputs(bh, s, d, seed)
+        p = C.normal_problem(bh, s, d, causal, 40 + seed, oracle_mod, std=0.7)
+        q, k, v = (torch.from_numpy(a).cuda() for a in (p.q, p.k, p.v))
         got = torch.full((bh * s * d,), float("nan"), device="cuda")
         want = torch.zeros(bh * s * d, device="cuda")
         before = lib.ncz_launch_count()
@@ -63,6 +66,7 @@ def test_no_alloc_entry_matches_allocating_entry_on_calls_in_a_row(ncz):
         assert lib.ncz_flash_fwd_splits(ctypes.byref(_desc(ncz, q, k, v, want, bh, s, d, causal)), 0) == 0
         assert ncz.sync_status() == 0
         assert bool(torch.isfinite(got).all())
+        C.check(got.cpu().numpy(), C.reference(p, oracle_mod), C.active_index(p), f"static {bh}x{s}x{d}")
         err = float((got - want).abs().max())
         assert err <= ATOL, (bh, s, d, causal, err)
 
