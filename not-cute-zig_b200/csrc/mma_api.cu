@@ -58,8 +58,20 @@ constexpr int kM = 16, kN = 8, kK = 16;
 constexpr uint32_t kTileA = kM * kK * 2;  // bytes of one A tile
 constexpr uint32_t kTileB = kK * kN * 2;  // bytes of one B tile
 constexpr int kChunk = 4;   // K tiles per stage
-constexpr int kStages = 4;
-constexpr int kWarps = 8;  // warps per CTA
+// Ring depth and warps per CTA: the throughput follows the warps resident per
+// SM (each warp's copies, waits and MMAs are a serial chain), as long as two
+// CTAs still fit the register file and shared memory.  Measured on B200 over
+// k_iters 1-40: 10 warps x 3 stages (2 x 90 KB, 20 warps per SM) 79-97 % of
+// the HBM copy bandwidth; 8 x 4 (16 warps) 68-87 %; deeper rings with fewer
+// warps lower still; 11-14 warps spill or hold one CTA per SM.
+#ifndef NCZM_STAGES
+#define NCZM_STAGES 3
+#endif
+#ifndef NCZM_WARPS
+#define NCZM_WARPS 10
+#endif
+constexpr int kStages = NCZM_STAGES;
+constexpr int kWarps = NCZM_WARPS;  // warps per CTA
 constexpr uint32_t kStageA = kChunk * kTileA;
 constexpr uint32_t kStageBytes = kStageA + kChunk * kTileB;
 constexpr uint32_t kWarpBytes = kStages * kStageBytes;
@@ -134,7 +146,10 @@ __device__ __forceinline__ float activate(float x, uint32_t kind) {
 // kBcol: B tiles column-major (element (k, n) at n * 16 + k: batched_mma_matmul,
 // mma_matmul), else row-major K x N (pipelined_mma_matmul).
 template <bool kBcol>
-__global__ void __launch_bounds__(kWarps * 32) mma_gemm(const __grid_constant__ MmaParams p) {
+#ifndef NCZM_MIN_BLOCKS
+#define NCZM_MIN_BLOCKS 2  // two CTAs per SM (the launch's grid assumes them)
+#endif
+__global__ void __launch_bounds__(kWarps * 32, NCZM_MIN_BLOCKS) mma_gemm(const __grid_constant__ MmaParams p) {
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = static_cast<int>(threadIdx.x >> 5), lane = static_cast<int>(threadIdx.x & 31);
     uint8_t *ring = smem + warp * kWarpBytes;
@@ -361,7 +376,7 @@ int launch(const nczm::MmaParams &p, void *stream) {
         }
         sms = g_sms[dev];
     }
-    // Two CTAs (16 warps, 2 x 98 KB of stages) per SM; warps stride over batches.
+    // Two CTAs (2 x kWarps warps and their stage rings) per SM; warps stride over batches.
     const long long need = (p.batches + nczm::kWarps - 1) / nczm::kWarps;
     const unsigned grid = static_cast<unsigned>(std::min<long long>(need, 2LL * sms));
     void *args[1] = {const_cast<nczm::MmaParams *>(&p)};

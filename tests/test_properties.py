@@ -139,7 +139,8 @@ def ref_gemm(ptrs_ok, k_iters, batches, strides):
        epilogue=st.integers(0, 7))
 def test_gemm_arguments_and_launch_shape(ncz, fake, ptrs_ok, k_iters, batches, strides, epilogue):
     """Under the fake devices: the status follows the rule, and a valid call
-    launches one mma_gemm<row_b> of min(ceil(batches / 8), 2 x SMs) CTAs."""
+    launches one mma_gemm<row_b> of min(ceil(batches / 10), 2 x SMs) CTAs of
+    10 warps."""
     lib = ncz.mma.lib()
     before = len(fake.launches)
     ptr = 0x1000_0000 if ptrs_ok else None
@@ -150,5 +151,5 @@ def test_gemm_arguments_and_launch_shape(ncz, fake, ptrs_ok, k_iters, batches, s
     new = fake.launches[before:]
     assert len(new) == launches
     if launches:
-        assert new[0].grid == min(-(-batches // 8), 2 * fake.sms) and new[0].block == 256
+        assert new[0].grid == min(-(-batches // 10), 2 * fake.sms) and new[0].block == 320
         assert ncz.driver.kernel_label(new[0].kernel) == "mma_gemm<row_b>"
