@@ -57,9 +57,12 @@ constexpr int kVariants = 12;  // (D in 16/32/64) x (TMA, LSU) x (f16, bf16 inpu
 // this many per SM: some SMs would idle, or take a second item while the rest
 // finish, and the longest item bounds the launch, so halving it pays (config
 // 2, 32 items: 22.9 -> 18.4 us; 160 causal items at S=8192: 104.5 -> 81.8 us).
-// From 1.5 items per SM up split-Q lost 4-14 %: each K/V tile then feeds one
-// pipeline instead of two (a split-Q K tile costs about 1.4 two-tile steps)
-// and the longest two-tile item no longer bounds the launch.  Splitting only
+// From 1.5 items per SM up split-Q lost 4-14 %: there are twice the items,
+// each with a fixed cost (Q load, first scores, a merge epilogue that holds
+// both pipelines) over half the K tiles, while a split-Q K tile alone costs
+// only 2-11 % more than a two-tile step (each K/V tile feeds one pipeline
+// instead of two), and the longest two-tile item no longer bounds the
+// launch.  Splitting only
 // the heaviest groups never gained more than 3 % over the better of none and
 // all in a sweep of 12 shapes, so the plan is all or nothing.
 #ifndef NCZ_QSPLIT_ITEMS_PER_SM
