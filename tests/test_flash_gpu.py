@@ -258,6 +258,30 @@ def test_host_pipeline_matches_device_launch(ncz, oracle_mod, qsplit_mode, chunk
             o_unit=2.0 ** -11 if o_dtype == "float16" else 0.0)
 
 
+@pytest.mark.parametrize("chunk", [0, 1, 3, 8])
+def test_host_pipeline_twin_items_match_device_launch(ncz, oracle_mod, chunk):
+    """seq_len <= 128 through ncz_flash_fwd_host: every chunk runs twin items
+    (two slices per item), chunks of an odd slice count end with an item of
+    one slice; the result equals the device-path launch bit for bit and meets
+    the parity bound."""
+    bh, s, d = 37, 100, 32
+    p = C.normal_problem(bh, s, d, True, 63, oracle_mod, std=0.7)
+    dev = torch.device("cuda:0")
+    q, k, v = (torch.from_numpy(a).to(dev) for a in (p.q, p.k, p.v))
+    opts = C_opts(p)
+    o_ref = torch.full((bh * s * d,), SENTINEL, dtype=torch.float32, device=dev)
+    ncz.launch_ex(q, k, v, o_ref, opts)
+    assert ncz.sync_status() == 0
+    qh, kh, vh = (torch.from_numpy(a).pin_memory() for a in (p.q, p.k, p.v))
+    oh = torch.full((bh * s * d,), SENTINEL, dtype=torch.float32).pin_memory()
+    qd, kd, vd, od = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v), torch.empty_like(o_ref)
+    ncz.launch_host(qh, kh, vh, oh, qd, kd, vd, od, opts, chunk_slices=chunk)
+    torch.cuda.synchronize()
+    assert ncz.sync_status() == 0
+    assert torch.equal(oh, o_ref.cpu())
+    C.check(oh.numpy(), C.reference(p, oracle_mod), C.active_index(p), f"host pipeline twin chunk={chunk}")
+
+
 SPLIT_CASES = [(4, 1024, 64, True), (3, 1000, 64, False), (2, 777, 32, True), (5, 1300, 16, True),
                (1, 4096, 64, True)]
 
