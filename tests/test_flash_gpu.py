@@ -417,16 +417,24 @@ def test_static_scratch_split_count_must_fit(ncz, oracle_mod, bh, splits, fits):
     assert torch.equal(a, b)
 
 
-def test_expired_wait_reports_device_timeout_and_context_survives(ncz, oracle_mod):
+@pytest.mark.parametrize("kind", ["split_q", "two_tile", "twin"])
+def test_expired_wait_reports_device_timeout_and_context_survives(ncz, oracle_mod, qsplit_mode, kind):
     """Failure detection without a GPU fault: with a short wait limit and the
     first scores never signalled (a barrier that nothing completes), the CTA
     aborts cleanly, ncz_flash_sync_status returns DeviceTimeout with the wait
     site (s_full = 5) in the status word, and the same context then runs a
-    correct launch."""
+    correct launch.  For each item kind: split-Q (one item of bh=1, S=200:
+    the merge hand-offs wait too), two Q tiles (split-Q off), twin (S=100,
+    three slices: two items)."""
     import ctypes
 
     lib = ncz.flash.lib()
-    p = C.normal_problem(1, 200, 64, True, 3, oracle_mod, std=0.6)
+    if kind == "twin":
+        p = C.normal_problem(3, 100, 64, True, 3, oracle_mod, std=0.6)
+    else:
+        p = C.normal_problem(1, 200, 64, True, 3, oracle_mod, std=0.6)
+    if kind == "two_tile":
+        qsplit_mode(2)
     assert lib.ncz_test_set_wait_limit(-1, 20_000_000) == 0  # about 10 ms
     assert lib.ncz_test_drop_arrive(-1, 1) == 0
     try:
